@@ -1,0 +1,464 @@
+"""Benchmark of the EXL3 decode hot path on B200.
+
+Default workload (the lna2 case): one routed-MoE decode
+layer -- hidden 4096, 256 experts with gate/up [4096 -> 2048] and down
+[2048 -> 4096], per-expert K in {2, 3} (p = 0.5), T = 4 tokens, router logits
+N(0,1) -> top-8 -> softmax over the 8, fp16 activations N(0,1), MCG codebook.
+A step is one layer over one batch of T tokens.  Steps cycle over --layers
+independent layers (seeded), so every step streams its experts from HBM:
+one layer's unique expert bytes (~240 MB at T = 4) already exceed the 126 MB
+L2, and the other layers stream through L2 between two uses of a layer.
+
+With --gpus N (torchrun, one rank per GPU) the layer is tensor-parallel:
+each rank holds the intermediate columns [r*2048/N, (r+1)*2048/N) of every
+expert's gate/up and those rows of down, computes a partial [T, 4096] and one
+NCCL all-reduce sums it.  Total work is fixed as N grows ("strong").
+
+metric/value: packed-weight bytes streamed per second (algorithmic bytes:
+unique experts' trellis + suh + svh of every rank's shard, plus activations),
+aggregated over ranks; us_per_layer is the step time.  `e2e` is the same
+metric through the public plugin call (vllm_exl3_c.lna2_moe_decode) with
+pinned host inputs copied in and the output copied back every step.
+
+--impl reference times the reference's own CPU decode + matmul
+(recipe-lna/lna2/bindings.cpp:16-101,135-148, built from source into
+oracle/_ref) on a bounded sample of the same workload, on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "routed-MoE decode layer: packed-weight HBM GB/s (config 2: T=4, top-8 of 256 experts, K2/K3, hidden 4096)"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+NCU_TRAFFIC_FILE = ROOT / "profiles" / "moe_kernel_config2_traffic.json"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--tokens", type=int, default=4)
+    ap.add_argument("--route", choices=["uniform", "zipf"], default="uniform")
+    ap.add_argument("--experts", type=int, default=256)
+    ap.add_argument("--precise", action="store_true", help="fp16-rounded weights in the MMA")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- env
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            v = float(json.loads(p.read_text())["hbm_gbs"])
+            return v, "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus = (bus_id or "").lower()
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.t is not None:
+            self.t.join(timeout=2)
+
+    def summary(self, t0: float, t1: float):
+        rows = []
+        for ts, line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            if self.bus and self.bus[-12:] not in f[1].lower():
+                continue
+            rows.append((ts, f))
+        inside = [f for ts, f in rows if t0 <= ts <= t1] or [f for ts, f in rows]
+        if not inside:
+            return None
+        sm = [float(f[2]) for f in inside if f[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for f in inside for i in range(4) if f[6 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(inside[0][3]) if inside[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(inside),
+                "in_region": any(t0 <= ts <= t1 for ts, _ in rows)}
+
+
+# ----------------------------------------------------------------------------- workload
+class MoeWorkload:
+    def __init__(self, args, rank, world, dev):
+        import torch
+
+        from dsv4_carve_b200 import synth
+        from dsv4_carve_b200 import vllm_exl3_c as ext
+
+        self.torch, self.ext, self.synth = torch, ext, synth
+        self.args, self.rank, self.world, self.dev = args, rank, world, dev
+        self.E, self.H, self.I_full, self.T, self.topk = args.experts, 4096, 2048, args.tokens, 8
+        self.I = self.I_full // world
+        self.layers, self.routes, self.xs, self.ubytes, self.uniq = [], [], [], [], []
+        for li in range(args.layers):
+            seed = 1000 + li
+            kbits = synth.expert_bits(self.E, seed)
+            L = synth.make_moe_layer(self.E, self.H, self.I_full, kbits, seed, device=dev, cb=synth.CB_MCG,
+                                     rank=rank, world=world)
+            if args.route == "zipf":
+                ids, w = synth.route_zipf(self.T, self.E, self.topk, seed=seed + 7, device=dev)
+            else:
+                ids, w = synth.route_uniform(self.T, self.E, self.topk, seed=seed + 7, device=dev)
+            x = synth.activations(self.T, self.H, seed=seed + 11, device=dev, dtype=torch.float16)
+            self.layers.append(L)
+            self.routes.append((ids, w))
+            self.xs.append(x)
+            act = self.T * self.H * 2 * 2   # x in, out written (fp16)
+            self.ubytes.append(L.unique_bytes(ids) + act)
+            self.uniq.append(int(torch.unique(ids).numel()))
+        self.kmax = 3
+        self.scratch = torch.zeros(ext.lna2_moe_scratch_bytes(self.T, self.topk, self.H, self.I), dtype=torch.uint8,
+                                   device=dev)
+        self.outs = [torch.empty((self.T, self.H), dtype=torch.float16, device=dev) for _ in self.layers]
+        ext.lna2_moe_prepare(self.kmax)
+        # pre-bound C-ABI calls for the device-resident path (no per-call Python checks)
+        from dsv4_carve_b200 import _lib
+
+        self._lib = _lib.load()
+        self._argv = []
+        for li, L in enumerate(self.layers):
+            ids, w = self.routes[li]
+            self._argv.append((self.xs[li].data_ptr(), _lib.DT_F16, self.outs[li].data_ptr(), _lib.DT_F16, self.T,
+                               self.H, self.I, *[t.data_ptr() for t in L.table_list()], self.E, L.ktab.data_ptr(),
+                               self.kmax, self.kmax, synth.CB_MCG, ids.data_ptr(), w.data_ptr(), self.topk,
+                               10.0, self.scratch.data_ptr(), self.scratch.numel(), int(args.precise)))
+        # pinned host copies for the end-to-end path
+        self.h_x = [x.cpu().pin_memory() for x in self.xs]
+        self.h_ids = [r[0].cpu().pin_memory() for r in self.routes]
+        self.h_w = [r[1].cpu().pin_memory() for r in self.routes]
+        self.h_out = [torch.empty((self.T, self.H), dtype=torch.float16).pin_memory() for _ in self.layers]
+        self.d_x = [torch.empty_like(x) for x in self.xs]
+        self.d_ids = [torch.empty_like(r[0]) for r in self.routes]
+        self.d_w = [torch.empty_like(r[1]) for r in self.routes]
+        self.h2d = self.xs[0].numel() * 2 + self.routes[0][0].numel() * 4 + self.routes[0][1].numel() * 4
+        self.d2h = self.T * self.H * 2
+
+    def launch(self, i, stream_handle):
+        rc = self._lib.exl3_moe_decode(*self._argv[i % len(self.layers)], stream_handle)
+        if rc:
+            raise RuntimeError(self._lib.exl3_last_error().decode())
+
+    def allreduce(self, out):
+        if self.world > 1:
+            self.torch.distributed.all_reduce(out)
+
+    def step(self, i, stream_handle):
+        self.launch(i, stream_handle)
+        self.allreduce(self.outs[i % len(self.layers)])
+
+    def e2e_step(self, i):
+        torch, ext = self.torch, self.ext
+        li = i % len(self.layers)
+        L = self.layers[li]
+        self.d_x[li].copy_(self.h_x[li], non_blocking=True)
+        self.d_ids[li].copy_(self.h_ids[li], non_blocking=True)
+        self.d_w[li].copy_(self.h_w[li], non_blocking=True)
+        out = self.outs[li]
+        ext.lna2_moe_decode(self.d_x[li], out, *L.table_list(), self.d_ids[li], self.d_w[li], self.kmax, 10.0,
+                            self.scratch, intermediate=self.I, k_table=L.ktab, codebook=L.cb,
+                            precise=self.args.precise)
+        self.allreduce(out)
+        self.h_out[li].copy_(out, non_blocking=True)
+
+    def bytes_per_step(self, i):
+        return self.ubytes[i % len(self.layers)]
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+_CPU_CACHE: dict = {}
+
+
+def _cpu_units(args):
+    """(expert, projection) units of layer 0 of the workload, in routed order,
+    with the rows each expert serves (config 2 routing, CPU generators)."""
+    from dsv4_carve_b200 import synth
+
+    key = (args.experts, args.tokens, args.route)
+    if key not in _CPU_CACHE:
+        E, T, topk, seed = args.experts, args.tokens, 8, 1000
+        kbits = synth.expert_bits(E, seed)
+        if args.route == "zipf":
+            ids, _ = synth.route_zipf(T, E, topk, seed=seed + 7)
+        else:
+            ids, _ = synth.route_uniform(T, E, topk, seed=seed + 7)
+        x = synth.activations(T, 4096, seed=seed + 11)
+        order = sorted(set(int(e) for e in ids.flatten().tolist()))
+        units = [(e, p, kbits[e], [r for r in range(T) if e in ids[r].tolist()])
+                 for e in order for p in ("gate", "up", "down")]
+        _CPU_CACHE[key] = (units, x)
+    return _CPU_CACHE[key]
+
+
+def cpu_reference_sample(args, seconds: float, start_unit: int = 0):
+    """The reference's CPU linear (recipe-lna/lna2/bindings.cpp:135-148:
+    dequant_cpu + at::mm) over 512-column slices of the routed experts'
+    gate/up/down matrices of config 2, until `seconds` of reference time have
+    been spent.  Weight generation is outside the timed calls.  Returns
+    (GB/s of packed bytes, sample description, cores, kind, seconds, units used)."""
+    import torch
+
+    from dsv4_carve_b200 import synth
+    from oracle import oracle as O
+
+    ref = O.ref_ext()
+    kind = "reference" if ref is not None else "port"
+    units, x = _cpu_units(args)
+    H, I, cols = 4096, 2048, 512
+    done_bytes, spent, n = 0, 0.0, 0
+    u = start_unit
+    while spent < seconds and n < 10000:
+        e, proj, K, rows = units[u % len(units)]
+        k = H if proj != "down" else I
+        g = synth._gen("cpu", 7919 * u + 1)
+        tr = synth.random_trellis(k // 16, cols // 16, K, g, "cpu")
+        su, sv = synth.random_signs(k, g, "cpu"), synth.random_svh(cols, g, "cpu")
+        xe = x[rows].contiguous() if proj != "down" else x[rows][:, :I].contiguous()
+        t0 = time.perf_counter()
+        if ref is not None:
+            ref.exl3_gemv(xe, tr, su, sv, K, True, 1)
+        else:
+            O.gemv(xe.numpy(), tr.numpy(), su.numpy(), sv.numpy(), K, 1)
+        spent += time.perf_counter() - t0
+        done_bytes += tr.numel() * 2 + su.numel() * 2 + sv.numel() * 2
+        n += 1
+        u += 1
+    sample = (f"{n} slices of {cols} output columns (MCG, K2/K3) from the gate/up/down matrices of the "
+              f"routed experts of a config-2 layer, each over the rows routed to its expert")
+    return done_bytes / spent / 1e9, sample, torch.get_num_threads(), kind, spent, n
+
+
+# ----------------------------------------------------------------------------- main
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    # each step: a bounded sample, sized so that the whole run stays near 2 minutes
+    per = max(0.3, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    desc = kind = None
+    cores = 1
+    unit = 0
+    for s in range(args.warmup + args.steps):
+        v, desc, cores, kind, _, used = cpu_reference_sample(args, per, unit)
+        unit += used
+        if s >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals) if vals else None
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "u16 trellis -> fp32",
+        "data": "synthetic", "config": {"workload": "config2_moe_decode_layer", "tokens": args.tokens, "topk": 8,
+                                        "experts": args.experts, "hidden": 4096, "intermediate": 2048},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"per step: {desc}; {per:.1f} s per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import datetime
+
+    import torch
+
+    rank, world, local = dist_env()
+    assert world == args.gpus or world == 1, "launch with torchrun for --gpus > 1"
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    wl = MoeWorkload(args, rank, world, dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    for i in range(args.warmup):
+        wl.step(i, sh)
+    torch.cuda.synchronize(dev)
+
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        bus = None
+    clocks = ClockSampler(bus) if (rank == 0 and not args.no_clocks) else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.6)
+
+    # ---- device-resident timed region
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_wall0 = time.time()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(K):
+        ev[i][0].record(stream)
+        wl.launch(i, sh)
+        ev[i][1].record(stream)
+        wl.allreduce(wl.outs[i % len(wl.layers)])
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t_wall1 = time.time()
+    ms = start.elapsed_time(end)
+    kern_ms = [a.elapsed_time(b) for a, b in ev]
+    my_bytes = sum(wl.bytes_per_step(i) for i in range(K))
+    t = torch.tensor([ms, float(my_bytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        tm = t[:1].clone()
+        torch.distributed.all_reduce(tm, op=torch.distributed.ReduceOp.MAX)
+        tb = t[1:].clone()
+        torch.distributed.all_reduce(tb)
+        ms_max, all_bytes = float(tm.item()), float(tb.item())
+    else:
+        ms_max, all_bytes = ms, float(my_bytes)
+
+    # ---- end-to-end through the public call with host buffers
+    e2e = None
+    if not args.no_e2e:
+        for i in range(min(3, args.warmup) or 1):
+            wl.e2e_step(i)
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for i in range(K):
+            wl.e2e_step(i)
+        e2.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms2 = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(ms2, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": all_bytes / (float(ms2.item()) / 1e3) / 1e9, "unit": UNIT,
+               "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
+               "ms_per_step": float(ms2.item()) / K, "api": "vllm_exl3_c.lna2_moe_decode"}
+
+    clock_info = None
+    if clocks:
+        clocks.stop()
+        clock_info = clocks.summary(t_wall0, t_wall1)
+
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    peak, peak_kind = measured_peak()
+    kern_avg_ms = statistics.mean(kern_ms)
+    bytes_per_launch = my_bytes / K
+    achieved = bytes_per_launch / (kern_avg_ms / 1e3) / 1e9
+    traffic = None
+    if NCU_TRAFFIC_FILE.exists() and world == 1:
+        try:
+            tr = json.loads(NCU_TRAFFIC_FILE.read_text())
+            traffic = tr.get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+    line = {
+        "metric": METRIC, "value": all_bytes / (ms_max / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
+        "steps": K, "warmup": args.warmup, "ms_per_step": ms_max / K, "us_per_layer": ms_max / K * 1e3,
+        "tokens_per_s_per_layer": args.tokens * K / (ms_max / 1e3),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "u16 trellis (K2/K3) -> fp16 MMA, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "config2_moe_decode_layer", "tokens": args.tokens, "topk": 8, "experts": args.experts,
+                   "hidden": 4096, "intermediate": 2048, "intermediate_per_gpu": 2048 // world,
+                   "route": args.route, "layers_cycled": args.layers,
+                   "unique_experts_per_layer": wl.uniq, "parallelism": f"tp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (unique bytes per layer > 126 MB; layers cycled)",
+                   "precise": bool(args.precise)},
+        "roofline": {"bound": "hbm", "kernel": "exl3::moe_kernel", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "kernel_us_avg": kern_avg_ms * 1e3},
+        "gpu_launches": K,
+        "e2e": e2e,
+        "clocks": clock_info,
+    }
+    if world == 1 and not args.no_cpu:
+        v, desc, cores, kind, dt, _ = cpu_reference_sample(args, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc,
+                                "seconds": dt}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,199 @@
+// common.cuh -- shared device helpers for the EXL3 B200 kernels (sm_100a).
+//
+// mbarrier / bulk-copy wrappers (inline PTX), bounded waits, error flags, and
+// the 128-point Walsh-Hadamard transform held as 4 values per lane of a warp.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace exl3 {
+
+// ---------------------------------------------------------------- errors
+// Device-side error bits, OR-ed into the scratch status word.  The kernels
+// never trap: a failed check records its bit and skips the work.
+enum : uint32_t {
+    ERR_DEP_TIMEOUT  = 1u << 0,   // a dependency counter did not reach its target
+    ERR_MISALIGNED   = 1u << 1,   // a trellis pointer is not 16-byte aligned
+    ERR_BAD_K        = 1u << 2,   // per-expert bit width outside the build's range
+    ERR_RING_TIMEOUT = 1u << 3,   // an mbarrier wait gave up
+    ERR_PLAN         = 1u << 4,   // route plan exceeded its capacity
+};
+
+// Every spin is bounded twice: by elapsed %globaltimer time (kWaitLimitNs)
+// and by an iteration cap, whichever comes first.  A wait that runs out
+// records its error bit and returns false; the caller abandons its work.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;    // 2 s
+constexpr uint32_t kSpinCap = 1u << 28;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void set_error(uint32_t* status, uint32_t bit) {
+    atomicOr(status, bit);
+}
+
+__device__ __forceinline__ bool aligned16_dev(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
+                 :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// try_wait that lets the hardware suspend the thread for up to ~20 us while the
+// phase is incomplete, so a waiting warp issues almost no instructions.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (after recording the error) if the phase never
+// completed.  Callers then abandon the CTA's remaining work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1; i < kSpinCap; ++i) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    set_error(status, ERR_RING_TIMEOUT);
+    return false;
+}
+
+// Warp-uniform bounded wait: lane 0 polls under the time bound, the verdict is
+// broadcast, then every lane observes the completed phase itself (one
+// try_wait that succeeds at once: the phase cannot advance again before this
+// warp releases the slot) so each lane gets the barrier's acquire ordering.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* status, int lane) {
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait(bar, parity, status);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok) {
+        for (int i = 0; i < 1024; ++i)
+            if (mbar_try_wait(bar, parity)) break;
+    }
+    return ok;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion counted in bytes
+// on an mbarrier.  No multicast (plain per-CTA copy).
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Named barrier over the consumer warps only (the producer warp never joins).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
+}
+
+// Named barrier that also ANDs a predicate over the participating threads,
+// so a give-up decision is taken by all of them together.
+__device__ __forceinline__ bool named_all(uint32_t id, uint32_t threads, bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+                 "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"((uint32_t) v), "r"(id), "r"(threads) : "memory");
+    return r != 0;
+}
+
+// ---------------------------------------------------------------- memory
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Spin (bounded) until *ctr >= target.  Returns false on timeout.
+__device__ __forceinline__ bool wait_counter(const uint32_t* ctr, uint32_t target, uint32_t* status) {
+    if (ld_acquire_u32(ctr) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1; i < kSpinCap; ++i) {
+        __nanosleep(64);
+        if (ld_acquire_u32(ctr) >= target) return true;
+        if ((i & 63u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    set_error(status, ERR_DEP_TIMEOUT);
+    return false;
+}
+
+// ---------------------------------------------------------------- numerics
+constexpr float kHadNorm = 0.088388347648318440550f;   // 1/sqrt(128)
+
+__device__ __forceinline__ uint32_t dup_half(__half h) {
+    const uint32_t b = __half_as_ushort(h);
+    return b | (b << 16);
+}
+
+// 128-point natural-order (Sylvester) Walsh-Hadamard transform over a warp:
+// lane l holds elements 4l..4l+3 in v[0..3].  Stages of stride 1 and 2 are in
+// registers, strides 4..64 pair lane l with lane l^(stride/4).  Each output is
+// the same sequence of fp32 additions as the textbook in-place butterfly with
+// strides 1, 2, 4, ..., 64.
+__device__ __forceinline__ void wht128_warp(float (&v)[4], int lane) {
+    float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+    v[0] = a0 + a2; v[1] = a1 + a3; v[2] = a0 - a2; v[3] = a1 - a3;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+            v[i] = upper ? (o - v[i]) : (v[i] + o);
+        }
+    }
+}
+
+__device__ __forceinline__ __half load_act_half(const void* x, int dtype, int64_t i) {
+    if (dtype == 0) return reinterpret_cast<const __half*>(x)[i];
+    if (dtype == 1) return __float2half_rn(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]));
+    return __float2half_rn(reinterpret_cast<const float*>(x)[i]);
+}
+
+__device__ __forceinline__ void store_out(void* out, int dtype, int64_t i, float v) {
+    if (dtype == 0) reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+    else if (dtype == 1) reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float*>(out)[i] = v;
+}
+
+}  // namespace exl3

@@ -1,0 +1,271 @@
+"""Drop-in for the reference's native extension module ``vllm_exl3_c``.
+
+Same entry-point names, positional argument order, argument meaning and
+error behaviour (RuntimeError with the reference's messages) as the
+pybind11 module the vllm-exl3 plugin imports through its ``NATIVE_SO`` hook
+(recipe-lna/lna2/bindings.cpp:178-224, recipe-lna/lna2/lna_moe_ticket.cu:489-581).
+Every call goes to the sm_100a kernels of libexl3b200.so on the tensors'
+CUDA device and the current stream; there is no CPU path (the reference's CPU
+fallback of dequant_trellis / exl3_gemv is its CPU baseline, not product).
+
+Generalisations over the reference, all optional keyword arguments:
+  * lna2_moe_decode(..., intermediate=256, k_table=None, codebook=1, precise=False):
+    any hidden / intermediate that are multiples of 128, top-k 1..16,
+    per-expert bit widths through an int32 [experts] table (K = largest);
+  * precise: round each decoded weight to fp16 before the MMA (the dense
+    entries default to True, the MoE to False; see include/exl3_b200.h);
+  * dequant_trellis / exl3_gemv / exl3_gemm(..., codebook=None): the
+    reference maps mcg=True to MCG and mcg=False to MUL1 (bindings.cpp:49);
+    ``codebook=0`` selects 3INST explicitly.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "dequant_trellis", "exl3_gemv", "exl3_gemm", "lna2_moe_decode", "lna2_moe_scratch_bytes",
+    "lna2_moe_max_rows", "lna2_moe_prepare", "lna2_moe_info", "lna2_moe_status",
+    "exl3_linear_scratch_bytes",
+]
+
+_DT = {torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16, torch.float32: _lib.DT_F32}
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _on_device:
+    """Make `device` current for the C-ABI call when it is not already."""
+
+    def __init__(self, device: torch.device):
+        self.index = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.index:
+            self.prev = cur
+            torch.cuda.set_device(self.index)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def _codebook(mcg: bool, codebook) -> int:
+    if codebook is None:
+        return _lib.CB_MCG if mcg else _lib.CB_MUL1
+    _check(int(codebook) in (0, 1, 2), "codebook must be 0 (3INST), 1 (MCG) or 2 (MUL1)")
+    return int(codebook)
+
+
+# --------------------------------------------------------------------- dequant
+def dequant_trellis(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int, mcg: bool,
+                    *, codebook: int | None = None, inner_only: bool = False) -> torch.Tensor:
+    """Decode an EXL3 trellis tensor into an fp16 weight matrix [in, out].
+
+    recipe-lna/lna2/bindings.cpp:118-133.  ``inner_only`` returns W' (no
+    Hadamards or sign vectors)."""
+    bits = int(K)
+    _check(1 <= bits <= 8, "K must be in 1..8")
+    _check(trellis.dim() == 3 and trellis.dtype == torch.int16,
+           "trellis must be int16 [rows/16, cols/16, 16*K]")
+    _check(trellis.size(2) == 16 * bits, "trellis last dimension must be 16*K")
+    _check(trellis.size(0) > 0 and trellis.size(1) > 0, "trellis dimensions must be positive")
+    _check(suh.dtype == torch.float16 and svh.dtype == torch.float16, "suh and svh must be float16")
+    _check(suh.numel() >= trellis.size(0) * 16 and svh.numel() >= trellis.size(1) * 16,
+           "suh/svh are too short")
+    _check(trellis.is_cuda, "dequant_trellis: the B200 build decodes on CUDA tensors only")
+    if not inner_only:
+        _check(trellis.size(0) % 8 == 0 and trellis.size(1) % 8 == 0,
+               "trellis dimensions must reconstruct whole 128-element Hadamard blocks")
+    t = trellis.contiguous()
+    su = suh.to(t.device).contiguous()
+    sv = svh.to(t.device).contiguous()
+    out = torch.empty((t.size(0) * 16, t.size(1) * 16), dtype=torch.float16, device=t.device)
+    with _on_device(t.device):
+        _lib.call("exl3_dequant", t.data_ptr(), t.size(0), t.size(1), bits, _codebook(mcg, codebook),
+                  su.data_ptr(), sv.data_ptr(), out.data_ptr(), 0 if inner_only else 1, _stream(t.device))
+    return out
+
+
+# --------------------------------------------------------------------- dense
+_LIN_SCRATCH: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def exl3_linear_scratch_bytes(rows: int, k: int, n: int, K: int) -> int:
+    return int(_lib.load().exl3_linear_scratch_bytes(rows, k, n, K))
+
+
+def _linear_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Shared per-(device, stream) linear scratch, zeroed on creation; the
+    kernel restores its control words, so it is reused without a memset."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, _stream(device))
+    buf = _LIN_SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes:
+        _check(not torch.cuda.is_current_stream_capturing(),
+               "exl3 linear scratch was not prewarmed for this device/stream (graph capture)")
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _LIN_SCRATCH[key] = buf
+    return buf
+
+
+def linear_forward(x2: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor,
+                   K: int, codebook: int, out_dtype: torch.dtype, precise: bool = True) -> torch.Tensor:
+    """y[m, n] = x2[m, k] . W on the current stream (k, n multiples of 128).
+
+    precise=True rounds every decoded weight to fp16 as the reference does;
+    False feeds the codebook's half pair to the tensor core unrounded."""
+    m, k = x2.shape
+    n = trellis.size(1) * 16
+    _check(x2.dtype in _DT and out_dtype in _DT, "exl3 linear: dtypes must be fp16, bf16 or fp32")
+    y = torch.empty((m, n), dtype=out_dtype, device=x2.device)
+    nbytes = exl3_linear_scratch_bytes(m, k, n, K)
+    scratch = _linear_scratch(x2.device, nbytes)
+    with _on_device(x2.device):
+        _lib.call("exl3_linear", x2.data_ptr(), _DT[x2.dtype], m, k, n, trellis.data_ptr(), K, codebook,
+                  suh.data_ptr(), svh.data_ptr(), y.data_ptr(), _DT[out_dtype], scratch.data_ptr(),
+                  scratch.numel(), int(bool(precise)), _stream(x2.device))
+    return y
+
+
+def _linear_checks(x, trellis, suh, svh, bits):
+    _check(x.dim() >= 2, "x must have shape [..., in_features]")
+    _check(x.size(-1) == trellis.size(0) * 16, "x feature dimension does not match trellis")
+    _check(trellis.dim() == 3 and trellis.dtype == torch.int16 and trellis.size(2) == 16 * bits,
+           "trellis must be int16 [rows/16, cols/16, 16*K]")
+    _check(suh.dtype == torch.float16 and svh.dtype == torch.float16, "suh and svh must be float16")
+    _check(x.is_cuda and trellis.is_cuda and suh.is_cuda and svh.is_cuda,
+           "exl3 linear: the B200 build runs on CUDA tensors only")
+    _check(x.device == trellis.device == suh.device == svh.device, "exl3 linear: tensors on different devices")
+
+
+def exl3_gemv(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+              mcg: bool, mmode: int = 1, *, codebook: int | None = None) -> torch.Tensor:
+    """Native small-m EXL3 GEMV, [m, k] -> [m, n] in x.dtype (bindings.cpp:135-148)."""
+    bits = int(K)
+    _check(x.dim() >= 2, "x must have shape [..., in_features]")
+    m = x.numel() // x.size(-1)
+    _check(1 <= m <= 8, "native GEMV supports 1 <= m <= 8")
+    _check(int(mmode) in (0, 1), "mmode must be 0 or 1")
+    _linear_checks(x, trellis, suh, svh, bits)
+    x2 = x.contiguous().view(m, x.size(-1))
+    return linear_forward(x2, trellis.contiguous(), suh.contiguous(), svh.contiguous(), bits,
+                          _codebook(mcg, codebook), x.dtype)
+
+
+def exl3_gemm(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+              mcg: bool, *, codebook: int | None = None) -> torch.Tensor:
+    """Native tiled EXL3 GEMM, any row count (bindings.cpp:104-109)."""
+    bits = int(K)
+    _linear_checks(x, trellis, suh, svh, bits)
+    x2 = x.contiguous().view(x.numel() // x.size(-1), x.size(-1))
+    return linear_forward(x2, trellis.contiguous(), suh.contiguous(), svh.contiguous(), bits,
+                          _codebook(mcg, codebook), x.dtype)
+
+
+# --------------------------------------------------------------------- MoE
+def lna2_moe_scratch_bytes(max_rows: int | None = None, topk: int = 8, hidden: int = 4096,
+                           intermediate: int = 2048) -> int:
+    """Scratch bytes for calls up to (max_rows, topk, hidden, intermediate).
+
+    With no arguments: the build's row ceiling, top-8, 4096 x 2048, which
+    covers every geometry of the plugin up to a single-GPU expert width."""
+    rows = lna2_moe_max_rows() if max_rows is None else int(max_rows)
+    return int(_lib.load().exl3_moe_scratch_bytes(rows, topk, hidden, intermediate))
+
+
+def lna2_moe_max_rows() -> int:
+    """Row ceiling of this build (the plugin asks, lna_moe_ticket.cu:491-492)."""
+    return int(_lib.load().exl3_moe_max_rows())
+
+
+def lna2_moe_prepare(K: int) -> None:
+    _check(1 <= int(K) <= 4, "LNA2 supports K1..K4 in this build")
+    _lib.call("exl3_moe_prepare", int(K))
+
+
+def lna2_moe_info(K: int) -> list[int]:
+    """14 ints; index 13 = concurrent streams (the plugin reads it, :1266-1273)."""
+    import ctypes
+
+    buf = (ctypes.c_int64 * 14)()
+    _lib.call("exl3_moe_info", int(K), ctypes.addressof(buf))
+    return [int(v) for v in buf]
+
+
+def lna2_moe_status(scratch: torch.Tensor, clear: bool = False) -> int:
+    """Device status word of a MoE scratch (0 = healthy).  Synchronizes."""
+    import ctypes
+
+    word = ctypes.c_uint32(0)
+    with _on_device(scratch.device):
+        _lib.call("exl3_scratch_status", scratch.data_ptr(), 1, int(bool(clear)), ctypes.addressof(word),
+                  _stream(scratch.device))
+    return int(word.value)
+
+
+def lna2_moe_decode(x: torch.Tensor, out: torch.Tensor,
+                    gate_trellis: torch.Tensor, gate_suh: torch.Tensor, gate_svh: torch.Tensor,
+                    up_trellis: torch.Tensor, up_suh: torch.Tensor, up_svh: torch.Tensor,
+                    down_trellis: torch.Tensor, down_suh: torch.Tensor, down_svh: torch.Tensor,
+                    expert_ids: torch.Tensor, routing_weights: torch.Tensor, K: int,
+                    swiglu_limit: float, scratch: torch.Tensor, *, intermediate: int = 256,
+                    k_table: torch.Tensor | None = None, codebook: int = 1,
+                    precise: bool = False) -> torch.Tensor:
+    """Routed-expert decode of one layer; writes and returns `out`.
+
+    Argument checks follow recipe-lna/lna2/lna_moe_ticket.cu:516-553."""
+    _check(x.is_cuda and x.dtype in (torch.float16, torch.bfloat16),
+           "LNA2 input must be CUDA fp16 or bf16")
+    _check(x.dim() == 2 and x.size(1) % 128 == 0, "LNA2 input must be [m,hidden] with hidden % 128 == 0")
+    max_m = lna2_moe_max_rows()
+    _check(1 <= x.size(0) <= max_m, "LNA2 row count out of range (1 <= m <= LNA2_MAX_M)")
+    _check(x.is_contiguous(), "LNA2 input must be contiguous")
+    _check(out.is_cuda and out.device == x.device and out.shape == x.shape and out.is_contiguous(),
+           "LNA2 output must match x shape/device and be contiguous")
+    _check(out.dtype in (torch.float16, torch.bfloat16, torch.float32), "LNA2 output must be fp16/bf16/fp32")
+    topk = expert_ids.size(-1) if expert_ids.dim() == 2 else -1
+    _check(expert_ids.is_cuda and expert_ids.dtype == torch.int32 and expert_ids.is_contiguous()
+           and expert_ids.dim() == 2 and expert_ids.size(0) == x.size(0) and 1 <= topk <= 16,
+           "LNA2 expert_ids must be contiguous int32 [m,topk]")
+    _check(routing_weights.is_cuda and routing_weights.dtype == torch.float32
+           and routing_weights.is_contiguous() and routing_weights.shape == expert_ids.shape,
+           "LNA2 routing_weights must be contiguous fp32 [m,topk]")
+    tables = (gate_trellis, gate_suh, gate_svh, up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh)
+    n_experts = gate_trellis.numel()
+    _check(1 <= n_experts <= 1024, "LNA2 pointer table has invalid expert count")
+    for t in tables:
+        _check(t.is_cuda and t.device == x.device and t.dtype == torch.int64 and t.is_contiguous()
+               and t.numel() == n_experts, "LNA2 pointer tables must be contiguous CUDA int64 [experts]")
+    limit = float(swiglu_limit)
+    _check(limit > 0.0 and limit < float("inf"), "LNA2 requires a finite positive SwiGLU limit")
+    inter = int(intermediate)
+    need = int(_lib.load().exl3_moe_scratch_bytes(x.size(0), topk, x.size(1), inter))
+    _check(scratch.is_cuda and scratch.device == x.device and scratch.dtype == torch.uint8
+           and scratch.is_contiguous() and scratch.numel() >= need, "LNA2 scratch too small")
+    if k_table is None:
+        bits = int(K)
+        _check(1 <= bits <= 4, "LNA2 supports K1..K4 in this build")
+        kt_ptr, kmax = None, bits
+    else:
+        _check(k_table.is_cuda and k_table.device == x.device and k_table.dtype == torch.int32
+               and k_table.is_contiguous() and k_table.numel() == n_experts,
+               "LNA2 k_table must be contiguous CUDA int32 [experts]")
+        kt_ptr, kmax = k_table.data_ptr(), int(K)
+        bits = kmax
+    with _on_device(x.device):
+        _lib.call("exl3_moe_decode", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                  x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
+                  kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
+                  scratch.data_ptr(), scratch.numel(), int(bool(precise)), _stream(x.device))
+    return out

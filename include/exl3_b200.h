@@ -1,0 +1,145 @@
+/*
+ * exl3_b200.h -- C ABI of the B200 (sm_100a) EXL3 decode hot path.
+ *
+ * Library: dsv4_carve_b200/libexl3b200.so.  Plain pointers, sizes and a CUDA
+ * stream (passed as void*, i.e. a cudaStream_t); no C++ or torch types.  All
+ * device pointers must be on the device that is current on the calling
+ * thread.  Every function returns EXL3_OK (0) or an exl3_status code; on
+ * failure exl3_last_error() returns a message for the calling thread.  Calls
+ * that launch work are asynchronous on `stream` and never allocate, copy or
+ * synchronize, so they may be captured in a CUDA graph once the per-device
+ * state has been prepared (exl3_*_prepare, or one eager call).
+ *
+ * Data formats (the EXL3 on-disk / in-memory layout used by the reference):
+ *   trellis  int16 [k/16, n/16, 16*K]   packed trellis words of W' (k = in, n = out)
+ *   suh      fp16  [k]                  input sign/scale vector
+ *   svh      fp16  [n]                  output sign/scale vector
+ *   W = diag(suh) . H . W' . H . diag(svh) / 128, H = 128-block Sylvester Hadamard.
+ * Codebooks: 0 = 3INST, 1 = MCG (the production codebook), 2 = MUL1.
+ * Activation / output dtypes: 0 = fp16, 1 = bf16, 2 = fp32.
+ *
+ * Each declaration cites the reference interface it replaces (paths relative
+ * to the lna-lab/dsv4-carve project root).
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    EXL3_OK = 0,
+    EXL3_ERR_ARG = 1,          /* invalid argument (shape, dtype, alignment, size) */
+    EXL3_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+    EXL3_ERR_UNSUPPORTED = 3,  /* valid input outside what this build implements */
+    EXL3_ERR_DEVICE = 4        /* the device-side status word reports a failure */
+} exl3_status;
+
+enum { EXL3_DTYPE_F16 = 0, EXL3_DTYPE_BF16 = 1, EXL3_DTYPE_F32 = 2 };
+enum { EXL3_CB_3INST = 0, EXL3_CB_MCG = 1, EXL3_CB_MUL1 = 2 };
+
+/* Version of this ABI (bumped on any signature change). */
+int exl3_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* exl3_last_error(void);
+
+/* ------------------------------------------------------------------ dequant
+ * Replaces vllm_exl3_c.dequant_trellis (recipe-lna/lna2/bindings.cpp:118-133,
+ * CPU dequant_cpu at :16-101) and the exllamav3_ext reconstruct call used by
+ * LinearEXL3.reconstruct_hgemm (recipe-lna/exllamav3/exl3.py.lna:161-218).
+ * full = 0: w = W' (inner decoded weights), fp16 [16*kt, 16*nt], bit-exact.
+ * full = 1: w = W  (both Hadamards and suh/svh applied in the reference's
+ *           float order), fp16.  suh/svh may be NULL when full = 0.
+ * K in 1..8; kt and nt multiples of 8 when full = 1. */
+int exl3_dequant(const void* trellis, int64_t kt, int64_t nt, int K, int cb,
+                 const void* suh, const void* svh, void* w, int full, void* stream);
+
+/* Arithmetic of the decode + MMA inner loop (`precise` argument below):
+ *   precise = 1: each weight is rounded to fp16, RN(lo + hi), exactly the
+ *                value the reference's decoder produces, before the fp16 MMA;
+ *   precise = 0: the codebook's (lo, hi) fp16 halves go to the tensor core
+ *                as one k-doubled element, so the weight enters as lo + hi
+ *                unrounded (one fewer rounding, fewer instructions).
+ * Both accumulate in fp32; they differ by the fp16 rounding of each weight. */
+
+/* ------------------------------------------------------------------ dense linear
+ * y[rows, n] = x[rows, k] . W   (GEMV form: input transform, decode + MMA,
+ * output transform).  Replaces vllm_exl3_c.exl3_gemv / exl3_gemm
+ * (recipe-lna/lna2/bindings.cpp:104-109,135-148), exllamav3_ext.exl3_gemm
+ * (recipe-lna/exllamav3/exl3_gemm.cu.lna:336-348) and
+ * BC_LinearEXL3.run_alloc as called by LinearEXL3.forward
+ * (recipe-lna/exllamav3/exl3.py.lna:114-139).
+ * k, n multiples of 128; K in 1..8; x row-major with leading dimension k,
+ * y row-major with leading dimension n.  Any rows >= 1 (processed in blocks
+ * of 32 rows).  `scratch` is a device buffer of at least
+ * exl3_linear_scratch_bytes(rows, k, n, K) bytes whose first
+ * EXL3_LINEAR_CTRL_BYTES bytes are zero before first use; the kernel leaves
+ * them zero again.  One launch at a time per scratch buffer. */
+#define EXL3_LINEAR_CTRL_BYTES 4096
+int64_t exl3_linear_scratch_bytes(int64_t rows, int64_t k, int64_t n, int K);
+int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n,
+                const void* trellis, int K, int cb, const void* suh, const void* svh,
+                void* y, int y_dtype, void* scratch, int64_t scratch_bytes, int precise,
+                void* stream);
+
+/* ------------------------------------------------------------------ routed MoE
+ * One routed-expert decode layer on one rank (TP shard of the intermediate
+ * dim): for every valid (row, slot), expert e = ids[row, slot]:
+ *   g = x . Wgate_e, u = x . Wup_e            (fp32, output transform applied)
+ *   a = fp16( silu(min(g, L)) * clamp(u, -L, L) )
+ *   d = a . Wdown_e                           (fp32)
+ *   out[row] = sum over slots, in slot order, of weights[row, slot] * d   (fp32),
+ * then one cast to out_dtype.  An expert listed twice in one row is computed
+ * once and added twice.  Ids outside [0, n_experts) are skipped.
+ * Replaces vllm_exl3_c.lna2_moe_decode (recipe-lna/lna2/lna_moe_ticket.cu:507-581)
+ * with its semantics (recipe-lna/vllm_exl3_exl3.py.lna:988-1027), generalised:
+ *   - pointer tables: device int64 [n_experts] arrays of device addresses,
+ *     in the reference's order gate/up/down x trellis/suh/svh; gate/up trellis
+ *     [hidden/16, inter/16, 16K], down trellis [inter/16, hidden/16, 16K];
+ *   - bits: k_table (device int32 [n_experts]) or, when k_table is NULL, the
+ *     scalar K for all experts; kmax = largest K present (1..4);
+ *   - m in 1..exl3_moe_max_rows(), topk in 1..16, m*topk <= 256,
+ *     hidden and inter multiples of 128, n_experts <= 1024;
+ *   - x fp16/bf16 [m, hidden]; out fp16/bf16/fp32 [m, hidden];
+ *     ids int32 [m, topk]; weights fp32 [m, topk] (routing scale included).
+ * `scratch`: >= exl3_moe_scratch_bytes(m, topk, hidden, inter) bytes, first
+ * EXL3_MOE_CTRL_BYTES zero before first use (the kernel restores them).  One
+ * launch at a time per scratch buffer. */
+#define EXL3_MOE_CTRL_BYTES 262144
+int64_t exl3_moe_scratch_bytes(int64_t m, int64_t topk, int64_t hidden, int64_t inter);
+/* Replaces lna2_moe_max_rows (recipe-lna/lna2/lna_moe_ticket.cu:491-492). */
+int64_t exl3_moe_max_rows(void);
+int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dtype,
+                    int64_t m, int64_t hidden, int64_t inter,
+                    const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
+                    const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
+                    const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh,
+                    int64_t n_experts, const int32_t* k_table, int K, int kmax, int cb,
+                    const int32_t* ids, const float* weights, int64_t topk,
+                    float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise,
+                    void* stream);
+/* Replaces lna2_moe_prepare (recipe-lna/lna2/lna_moe_ticket.cu:494-500):
+ * occupancy, grid and kernel attributes for the current device, cached, so
+ * that later calls can be captured in a CUDA graph. */
+int exl3_moe_prepare(int kmax);
+/* Replaces lna2_moe_info (recipe-lna/lna2/lna_moe_ticket.cu:502-513): fills
+ * info[14] = {sms, resident CTAs/SM, warps/CTA, grid, threads, codebook count,
+ * ring stages, max rows, static smem bytes, ctrl bytes, scratch bytes for
+ * (max rows, topk 8, 4096, 2048), max rows, max pairs, concurrent streams}. */
+int exl3_moe_info(int kmax, int64_t* info);
+
+/* Device status word of a scratch buffer (MoE or linear): bit 0 dependency
+ * wait timed out, bit 1 misaligned trellis pointer, bit 2 bit width out of
+ * range, bit 3 ring wait timed out, bit 4 route plan overflow.  Synchronizes
+ * `stream`; not for use during graph capture.  clear != 0 resets the word.
+ * No counterpart in the reference, whose kernels cannot report errors. */
+int exl3_scratch_status(void* scratch, int is_moe, int clear, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
