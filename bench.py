@@ -90,7 +90,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, bus_id: str | None):
-        self.bus = (bus_id or "").lower()
+        self.bus = str(bus_id or "").lower()   # "bb:dd.0" suffix of nvidia-smi's pci.bus_id
         self.proc = None
         self.lines: list[str] = []
         self.t = None
@@ -125,7 +125,7 @@ class ClockSampler:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 10:
                 continue
-            if self.bus and self.bus[-12:] not in f[1].lower():
+            if self.bus and not f[1].lower().endswith(self.bus):
                 continue
             rows.append((ts, f))
         inside = [f for ts, f in rows if t0 <= ts <= t1] or [f for ts, f in rows]
@@ -350,7 +350,8 @@ def main():
 
     bus = None
     try:
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+        pr = torch.cuda.get_device_properties(dev)
+        bus = f"{int(pr.pci_bus_id):02x}:{int(pr.pci_device_id):02x}.0"
     except Exception:
         bus = None
     clocks = ClockSampler(bus) if (rank == 0 and not args.no_clocks) else None

@@ -137,6 +137,18 @@ uint16_t exo_codebook(uint32_t window, int cb, int trunc) {
     return trunc ? exo_half_from_float_trunc((float) v) : exo_half_from_double(v);
 }
 
+/* The codebook value before any fp16 rounding: lo + hi exactly for 3INST /
+ * MCG (the form the fast GEMV path feeds to the tensor core), the fp16
+ * result for MUL1 (which has a single value). */
+double exo_codebook_exact(uint32_t window, int cb) {
+    if (cb == 2) return (double) exo_half_to_float(exo_codebook(window, 2, 0));
+    uint32_t x = window & 0xffffu;
+    if (cb == 0) x = x * 89226354u + 64248484u;
+    else         x = x * 0xCBAC1FEDu;
+    x = lop3_6a(x, 0x8fff8fffu, 0x3b603b60u);
+    return (double) exo_half_to_float((uint16_t) (x & 0xffffu)) + (double) exo_half_to_float((uint16_t) (x >> 16));
+}
+
 /* ----------------------------------------------------------- tile layout */
 
 /* Lane l decodes weights t = 8l .. 8l+7 of a tile; weight t lands at
@@ -162,6 +174,24 @@ void exo_decode(const int16_t* trellis, int64_t kt, int64_t nt, int K, int cb,
             }
         }
     }
+}
+
+/* W' as doubles: the fp16-rounded weights (exact = 0) or lo + hi (exact = 1). */
+static double* decode_values(const int16_t* trellis, int64_t kt, int64_t nt, int K, int cb, int exact) {
+    const int64_t cols = nt * 16;
+    double* w = (double*) malloc(sizeof(double) * (size_t) (kt * 16 * cols));
+    for (int64_t a = 0; a < kt; ++a)
+        for (int64_t b = 0; b < nt; ++b) {
+            const uint16_t* tile = (const uint16_t*) (trellis + (a * nt + b) * 16 * K);
+            for (int t = 0; t < 256; ++t) {
+                int k, n;
+                tile_position(t, &k, &n);
+                const uint32_t win = exo_window(tile, K, t);
+                w[(a * 16 + k) * cols + b * 16 + n] =
+                    exact ? exo_codebook_exact(win, cb) : (double) exo_half_to_float(exo_codebook(win, cb, 0));
+            }
+        }
+    return w;
 }
 
 /* ---------------------------------------------------------------- hadamard */
@@ -233,18 +263,16 @@ void exo_input_transform(const void* x, int x_dtype, int64_t R, int64_t k,
 }
 
 /* y[R, n] = out_transform( xh[R, k] . W'[k, n] ), all in double. */
-static void gemv_core(const uint16_t* xh, int64_t R, const uint16_t* wprime,
+static void gemv_core(const uint16_t* xh, int64_t R, const double* wprime,
                       const uint16_t* svh, int64_t k, int64_t n, double* y) {
-    double* wf = (double*) malloc(sizeof(double) * (size_t) n);
     for (int64_t r = 0; r < R; ++r) {
         double* yr = y + r * n;
         for (int64_t c = 0; c < n; ++c) yr[c] = 0.0;
         for (int64_t i = 0; i < k; ++i) {
             const double a = (double) exo_half_to_float(xh[r * k + i]);
             if (a == 0.0) continue;
-            const uint16_t* wrow = wprime + i * n;
-            for (int64_t c = 0; c < n; ++c) wf[c] = (double) exo_half_to_float(wrow[c]);
-            for (int64_t c = 0; c < n; ++c) yr[c] += a * wf[c];
+            const double* wrow = wprime + i * n;
+            for (int64_t c = 0; c < n; ++c) yr[c] += a * wrow[c];
         }
         for (int64_t b = 0; b < n; b += 128) {
             fwht_double(yr + b, 128);
@@ -252,38 +280,39 @@ static void gemv_core(const uint16_t* xh, int64_t R, const uint16_t* wprime,
                 yr[b + i] = yr[b + i] * kNormD * (double) exo_half_to_float(svh[b + i]);
         }
     }
-    free(wf);
 }
 
-void exo_gemv(const void* x, int x_dtype, int64_t R, const int16_t* trellis,
-              const uint16_t* suh, const uint16_t* svh, int64_t k, int64_t n,
-              int K, int cb, double* y) {
-    uint16_t* wp = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) (k * n));
+void exo_gemv_ex(const void* x, int x_dtype, int64_t R, const int16_t* trellis,
+                 const uint16_t* suh, const uint16_t* svh, int64_t k, int64_t n,
+                 int K, int cb, int exact, double* y) {
+    double* wp = decode_values(trellis, k / 16, n / 16, K, cb, exact);
     uint16_t* xh = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) (R * k));
-    exo_decode(trellis, k / 16, n / 16, K, cb, 0, wp);
     exo_input_transform(x, x_dtype, R, k, suh, xh);
     gemv_core(xh, R, wp, svh, k, n, y);
     free(xh);
     free(wp);
 }
 
+void exo_gemv(const void* x, int x_dtype, int64_t R, const int16_t* trellis,
+              const uint16_t* suh, const uint16_t* svh, int64_t k, int64_t n,
+              int K, int cb, double* y) {
+    exo_gemv_ex(x, x_dtype, R, trellis, suh, svh, k, n, K, cb, 0, y);
+}
+
 /* --------------------------------------------------------------------- MoE */
 
-int64_t exo_moe(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
-                const int16_t* const* gt, const uint16_t* const* gsu, const uint16_t* const* gsv,
-                const int16_t* const* ut, const uint16_t* const* usu, const uint16_t* const* usv,
-                const int16_t* const* dt, const uint16_t* const* dsu, const uint16_t* const* dsv,
-                const int32_t* Ktab, int cb, int64_t E,
-                const int32_t* ids, const float* weights, int64_t topk,
-                double limit, double* out) {
+int64_t exo_moe_ex(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
+                   const int16_t* const* gt, const uint16_t* const* gsu, const uint16_t* const* gsv,
+                   const int16_t* const* ut, const uint16_t* const* usu, const uint16_t* const* usv,
+                   const int16_t* const* dt, const uint16_t* const* dsu, const uint16_t* const* dsv,
+                   const int32_t* Ktab, int cb, int64_t E,
+                   const int32_t* ids, const float* weights, int64_t topk,
+                   double limit, int exact, double* out) {
     /* dc[r][slot] keeps each row's expert output per slot; duplicated
      * (expert,row) slots reuse the same computed pair. */
     double* dc = (double*) calloc((size_t) (T * topk * H), sizeof(double));
     int64_t pairs = 0;
     const int64_t L = H > I ? H : I;
-    uint16_t* wg = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) (H * I));
-    uint16_t* wu = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) (H * I));
-    uint16_t* wd = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) (H * I));
     uint16_t* xh = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) L);
     uint16_t* act = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) I);
     double* g = (double*) malloc(sizeof(double) * (size_t) I);
@@ -295,9 +324,9 @@ int64_t exo_moe(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
         for (int64_t s = 0; s < T * topk; ++s) used |= ids[s] == e;
         if (!used) continue;
         const int K = Ktab[e];
-        exo_decode(gt[e], H / 16, I / 16, K, cb, 0, wg);
-        exo_decode(ut[e], H / 16, I / 16, K, cb, 0, wu);
-        exo_decode(dt[e], I / 16, H / 16, K, cb, 0, wd);
+        double* wg = decode_values(gt[e], H / 16, I / 16, K, cb, exact);
+        double* wu = decode_values(ut[e], H / 16, I / 16, K, cb, exact);
+        double* wd = decode_values(dt[e], I / 16, H / 16, K, cb, exact);
         for (int64_t r = 0; r < T; ++r) {
             int64_t first = -1;
             for (int64_t s = 0; s < topk; ++s)
@@ -322,6 +351,7 @@ int64_t exo_moe(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
             for (int64_t s = 0; s < topk; ++s)
                 if (ids[r * topk + s] == e) memcpy(dc + (r * topk + s) * H, d, sizeof(double) * (size_t) H);
         }
+        free(wd); free(wu); free(wg);
     }
     for (int64_t r = 0; r < T; ++r) {
         double* o = out + r * H;
@@ -334,6 +364,17 @@ int64_t exo_moe(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
             for (int64_t c = 0; c < H; ++c) o[c] += wv * src[c];
         }
     }
-    free(d); free(u); free(g); free(act); free(xh); free(wd); free(wu); free(wg); free(dc);
+    free(d); free(u); free(g); free(act); free(xh); free(dc);
     return pairs;
+}
+
+int64_t exo_moe(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
+                const int16_t* const* gt, const uint16_t* const* gsu, const uint16_t* const* gsv,
+                const int16_t* const* ut, const uint16_t* const* usu, const uint16_t* const* usv,
+                const int16_t* const* dt, const uint16_t* const* dsu, const uint16_t* const* dsv,
+                const int32_t* Ktab, int cb, int64_t E,
+                const int32_t* ids, const float* weights, int64_t topk,
+                double limit, double* out) {
+    return exo_moe_ex(x, x_dtype, T, H, I, gt, gsu, gsv, ut, usu, usv, dt, dsu, dsv, Ktab, cb, E,
+                      ids, weights, topk, limit, 0, out);
 }

@@ -50,6 +50,10 @@ uint32_t exo_window(const uint16_t* tile, int K, int t);
 /* Codebook value of a window as fp16 bits.  cb: 0 3INST, 1 MCG, 2 MUL1. */
 uint16_t exo_codebook(uint32_t window, int cb, int trunc);
 
+/* Codebook value with no fp16 rounding: lo + hi for 3INST / MCG (what the
+ * fast GEMV path multiplies by), the fp16 value for MUL1. */
+double exo_codebook_exact(uint32_t window, int cb);
+
 /* Decode a packed trellis [kt, nt, 16K] int16 into W' [16kt, 16nt] fp16 bits
  * (row = input feature k, column = output feature n). */
 void exo_decode(const int16_t* trellis, int64_t kt, int64_t nt, int K, int cb,
@@ -69,6 +73,12 @@ void exo_gemv(const void* x, int x_dtype, int64_t R, const int16_t* trellis,
               const uint16_t* suh, const uint16_t* svh, int64_t k, int64_t n,
               int K, int cb, double* y);
 
+/* exo_gemv with exact = 1: weights enter as lo + hi unrounded (the fast
+ * kernel path's arithmetic); exact = 0 is exo_gemv. */
+void exo_gemv_ex(const void* x, int x_dtype, int64_t R, const int16_t* trellis,
+                 const uint16_t* suh, const uint16_t* svh, int64_t k, int64_t n,
+                 int K, int cb, int exact, double* y);
+
 /* Routed-MoE decode layer (one rank).  Per-expert tables are host arrays of
  * host pointers.  ids [T, topk] int32 (ids outside [0, E) are skipped),
  * weights [T, topk] fp32, out [T, H] double.  Ktab[e] is the bit width of
@@ -80,6 +90,15 @@ int64_t exo_moe(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
                 const int32_t* Ktab, int cb, int64_t E,
                 const int32_t* ids, const float* weights, int64_t topk,
                 double limit, double* out);
+
+/* exo_moe with the weight rounding mode of exo_gemv_ex. */
+int64_t exo_moe_ex(const void* x, int x_dtype, int64_t T, int64_t H, int64_t I,
+                   const int16_t* const* gt, const uint16_t* const* gsu, const uint16_t* const* gsv,
+                   const int16_t* const* ut, const uint16_t* const* usu, const uint16_t* const* usv,
+                   const int16_t* const* dt, const uint16_t* const* dsu, const uint16_t* const* dsv,
+                   const int32_t* Ktab, int cb, int64_t E,
+                   const int32_t* ids, const float* weights, int64_t topk,
+                   double limit, int exact, double* out);
 
 #ifdef __cplusplus
 }

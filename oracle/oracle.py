@@ -42,9 +42,14 @@ def lib() -> C.CDLL:
         L.exo_input_transform.argtypes = [_P, C.c_int, _I64, _I64, _P, _P]
         L.exo_gemv.restype = None
         L.exo_gemv.argtypes = [_P, C.c_int, _I64, _P, _P, _P, _I64, _I64, C.c_int, C.c_int, _P]
+        L.exo_gemv_ex.restype = None
+        L.exo_gemv_ex.argtypes = [_P, C.c_int, _I64, _P, _P, _P, _I64, _I64, C.c_int, C.c_int, C.c_int, _P]
         L.exo_moe.restype = _I64
         L.exo_moe.argtypes = ([_P, C.c_int, _I64, _I64, _I64] + [_P] * 9
                               + [_P, C.c_int, _I64, _P, _P, _I64, C.c_double, _P])
+        L.exo_moe_ex.restype = _I64
+        L.exo_moe_ex.argtypes = ([_P, C.c_int, _I64, _I64, _I64] + [_P] * 9
+                                 + [_P, C.c_int, _I64, _P, _P, _I64, C.c_double, C.c_int, _P])
         _lib = L
     return _lib
 
@@ -123,20 +128,23 @@ def input_transform(x: np.ndarray, suh: np.ndarray, dtype_code: int | None = Non
 
 
 def gemv(x: np.ndarray, trellis: np.ndarray, suh: np.ndarray, svh: np.ndarray, K: int,
-         cb: int = CB_MCG, dtype_code: int | None = None) -> np.ndarray:
-    """Dense EXL3 linear in GEMV form; returns float64 [R, n]."""
+         cb: int = CB_MCG, dtype_code: int | None = None, exact: bool = False) -> np.ndarray:
+    """Dense EXL3 linear in GEMV form; returns float64 [R, n].
+
+    exact=False multiplies by the fp16-rounded weights (the reference's
+    decoder); exact=True by lo + hi unrounded (the fast kernel path)."""
     xa, code = _act(x, dtype_code)
     R, k = xa.shape
     t = _bits16(trellis)
     n = t.shape[1] * 16
     y = np.empty((R, n), dtype=np.float64)
-    lib().exo_gemv(_ptr(xa), code, R, _ptr(t), _ptr(_bits16(suh)), _ptr(_bits16(svh)), k, n, K, cb,
-                   _ptr(y))
+    lib().exo_gemv_ex(_ptr(xa), code, R, _ptr(t), _ptr(_bits16(suh)), _ptr(_bits16(svh)), k, n, K, cb,
+                      int(exact), _ptr(y))
     return y
 
 
 def moe(x: np.ndarray, experts: list[dict], Ktab, ids: np.ndarray, weights: np.ndarray,
-        limit: float, cb: int = CB_MCG, dtype_code: int | None = None):
+        limit: float, cb: int = CB_MCG, dtype_code: int | None = None, exact: bool = False):
     """Routed-MoE decode layer.  experts[e] has keys gate/up/down -> (trellis, suh, svh).
 
     Returns (out float64 [T, H], number of unique (expert,row) pairs).
@@ -158,8 +166,9 @@ def moe(x: np.ndarray, experts: list[dict], Ktab, ids: np.ndarray, weights: np.n
     weights = np.ascontiguousarray(weights, dtype=np.float32)
     topk = ids.shape[1]
     out = np.empty((T, H), dtype=np.float64)
-    pairs = lib().exo_moe(_ptr(xa), code, T, H, I, *[C.cast(t, C.c_void_p) for t in tabs],
-                          _ptr(ktab), cb, E, _ptr(ids), _ptr(weights), topk, float(limit), _ptr(out))
+    pairs = lib().exo_moe_ex(_ptr(xa), code, T, H, I, *[C.cast(t, C.c_void_p) for t in tabs],
+                             _ptr(ktab), cb, E, _ptr(ids), _ptr(weights), topk, float(limit), int(exact),
+                             _ptr(out))
     return out, int(pairs)
 
 

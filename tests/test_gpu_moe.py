@@ -6,6 +6,9 @@ boundary rows, inputs zero / unit / amplified past the SwiGLU clamp,
 bitwise determinism over two runs, NaN-poisoned scratch replay, and the
 device status word.  Tolerances: fp32 output max-abs <= 2e-3 against the
 oracle's fp64 result on unit-scale inputs and per-row relative <= 2e-3.
+The fast path (precise=False, lo + hi unrounded in the MMA) is compared with
+the oracle in the same arithmetic (exact=True); precise=True with the
+fp16-rounded reference weights.
 """
 from __future__ import annotations
 
@@ -53,9 +56,10 @@ def run_kernel(L, x, ids, w, limit=10.0, out_dtype=torch.float32, precise=False,
     return out, scratch
 
 
-def run_oracle(oracle, L, x, ids, w, limit=10.0):
+def run_oracle(oracle, L, x, ids, w, limit=10.0, exact=True):
     xa, code = oracle_x(x)
-    return oracle.moe(xa, moe_np(L), L.kbits, ids.numpy(), w.numpy(), limit, cb=L.cb, dtype_code=code)
+    return oracle.moe(xa, moe_np(L), L.kbits, ids.numpy(), w.numpy(), limit, cb=L.cb, dtype_code=code,
+                      exact=exact)
 
 
 def check(got, want):
@@ -72,9 +76,12 @@ def test_small_mixed_k(cuda, oracle, cb, precise):
     ids, w = synth.route_uniform(T, E, topk, seed=5)
     x = synth.activations(T, H, seed=6)
     got, scratch = run_kernel(to_device(L0, cuda), x, ids, w, precise=precise)
-    want, _ = run_oracle(oracle, L0, x, ids, w)
+    want, _ = run_oracle(oracle, L0, x, ids, w, exact=not precise)
     check(got, want)
     assert ext.lna2_moe_status(scratch) == 0
+    if not precise:
+        rounded, _ = run_oracle(oracle, L0, x, ids, w, exact=False)
+        assert row_rel(got.cpu().numpy(), rounded) <= 2e-3
 
 
 @pytest.mark.parametrize("profile", ["unique", "hot", "zipf", "dup", "invalid", "single"])
