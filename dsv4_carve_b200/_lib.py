@@ -19,6 +19,7 @@ DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
 LINEAR_CTRL_BYTES = 4096
 MOE_CTRL_BYTES = 262144
+MOE_STATIC_SCRATCH_BYTES = 4 << 20
 
 _P = C.c_void_p
 _I64 = C.c_int64
@@ -35,6 +36,8 @@ _SIGS = {
     "exl3_moe_max_rows": (_I64, []),
     "exl3_moe_decode": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
                         + [_I64, _P, _I, _I, _I, _P, _P, _I64, C.c_float, _P, _I64, _I, _P]),
+    "exl3_moe_decode_noalloc": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
+                                + [_I64, _P, _I, _I, _I, _P, _P, _I64, C.c_float, _I, _P]),
     "exl3_moe_prepare": (_I, [_I]),
     "exl3_moe_info": (_I, [_I, _P]),
     "exl3_scratch_status": (_I, [_P, _I, _I, _P, _P]),

@@ -716,3 +716,69 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     EXL3_CUDA(cudaGetLastError());
     return EXL3_OK;
 }
+
+// ------------------------------------------------------------------ allocation-free variant
+// exl3_moe_decode_noalloc: the same layer as exl3_moe_decode for callers that
+// may not allocate device memory at all -- code running while a CUDA graph is
+// being captured (an allocation there is either illegal or baked into the
+// graph), hosts whose memory is owned by another allocator and who therefore
+// cannot hand out a scratch buffer, and latency-critical callers that cannot
+// afford cudaMalloc's implicit synchronization.  Its scratch is the array
+// below, compiled into the library: EXL3_MOE_STATIC_SCRATCH_BYTES (4 MiB) of
+// device memory that every GPU which loads the library holds until the
+// process exits.  Geometries whose scratch (exl3_moe_scratch_bytes) exceeds it
+// are rejected.
+namespace exl3 {
+namespace {
+
+static __device__ __align__(256) uint8_t g_moe_static_scratch[EXL3_MOE_STATIC_SCRATCH_BYTES];
+
+// Device address of g_moe_static_scratch, looked up once per device with that
+// device current (in host code the array's name is only a host-side stand-in).
+std::mutex g_static_mu;
+void* g_static_ptr[64] = {};
+
+int static_scratch_ptr(int dev, void** out) {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        EXL3_CUDA(cudaGetSymbolAddress(&p, g_moe_static_scratch));
+        EXL3_REQUIRE(p != nullptr && aligned16(p), EXL3_ERR_CUDA, "moe noalloc: static scratch has no device address");
+        g_static_ptr[dev] = p;
+    }
+    *out = g_static_ptr[dev];
+    return EXL3_OK;
+}
+
+}  // namespace
+}  // namespace exl3
+
+extern "C" int exl3_moe_decode_noalloc(const void* x, int x_dtype, void* out, int out_dtype, int64_t m,
+                                       int64_t hidden, int64_t inter, const int64_t* gate_trellis,
+                                       const int64_t* gate_suh, const int64_t* gate_svh, const int64_t* up_trellis,
+                                       const int64_t* up_suh, const int64_t* up_svh, const int64_t* down_trellis,
+                                       const int64_t* down_suh, const int64_t* down_svh, int64_t n_experts,
+                                       const int32_t* k_table, int K, int kmax, int cb, const int32_t* ids,
+                                       const float* weights, int64_t topk, float swiglu_limit, int precise,
+                                       void* stream) {
+    EXL3_REQUIRE(m >= 1 && topk >= 1 && hidden >= 128 && inter >= 128, EXL3_ERR_ARG,
+                 "moe noalloc: row count, topk, hidden and intermediate must be positive");
+    const int64_t need = exl3_moe_scratch_bytes(m, topk, hidden, inter);
+    EXL3_REQUIRE(need > 0 && need <= EXL3_MOE_STATIC_SCRATCH_BYTES, EXL3_ERR_ARG,
+                 "moe noalloc: this geometry needs %lld scratch bytes, more than the static maximum of %d "
+                 "(use exl3_moe_decode with a caller-provided scratch)",
+                 (long long) need, (int) EXL3_MOE_STATIC_SCRATCH_BYTES);
+    int dev = 0;
+    EXL3_CUDA(cudaGetDevice(&dev));
+    EXL3_REQUIRE(dev >= 0 && dev < 64, EXL3_ERR_UNSUPPORTED, "moe noalloc: device index >= 64");
+    void* scratch = nullptr;
+    if (int rc = exl3::static_scratch_ptr(dev, &scratch)) return rc;
+    // The array keeps the previous call's contents; the control region (ticket
+    // and retire counters, status word, completion counters) must be zero.
+    auto s = static_cast<cudaStream_t>(stream);
+    EXL3_CUDA(cudaMemsetAsync(scratch, 0, EXL3_MOE_CTRL_BYTES, s));
+    return exl3_moe_decode(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
+                           up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K,
+                           kmax, cb, ids, weights, topk, swiglu_limit, scratch, EXL3_MOE_STATIC_SCRATCH_BYTES,
+                           precise, stream);
+}
