@@ -19,7 +19,7 @@ DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
 LINEAR_CTRL_BYTES = 4096
 MOE_CTRL_BYTES = 262144
-MOE_STATIC_SCRATCH_BYTES = 4 << 20
+MOE_STATIC_SCRATCH_BYTES = 8 << 20
 
 _P = C.c_void_p
 _I64 = C.c_int64

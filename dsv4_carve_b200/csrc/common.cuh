@@ -113,6 +113,56 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, u
     return ok;
 }
 
+// Bounded wait polled by every lane of a warp (each lane gets the barrier's
+// acquire ordering itself); the verdict is made warp-uniform.
+__device__ __forceinline__ bool mbar_wait_lanes(uint64_t* bar, uint32_t parity, uint32_t* status) {
+    bool ok = mbar_try_wait(bar, parity);
+    if (!ok) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t i = 1; i < kSpinCap; ++i) {
+            if (mbar_try_wait_sleep(bar, parity)) { ok = true; break; }
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && (threadIdx.x & 31) == 0) set_error(status, ERR_RING_TIMEOUT);
+    return ok;
+}
+
+// Orders this thread's generic-proxy accesses to global memory with its
+// async-proxy (bulk copy) accesses: used after writing data that another
+// CTA's bulk copy will read, and after acquiring it before issuing the copy.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// 3-D tiled TMA load of one box into this CTA's shared memory, completion
+// counted in bytes on an mbarrier.  No multicast.  The innermost coordinate
+// is always 0 here (whole 16-bit tiles), so it is 16-byte aligned.
+__device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(smem_u32(dst_smem)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Device-side tensor-map update: replace the global address of a tensor map
+// held in shared memory (128-byte aligned), publish it to its global slot
+// with the tensormap-proxy release (all 32 lanes), acquire it before use.
+__device__ __forceinline__ void tmap_replace_address(void* smem_tmap, const void* gaddr) {
+    asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;"
+                 :: "r"(smem_u32(smem_tmap)), "l"(gaddr) : "memory");
+}
+
+__device__ __forceinline__ void tmap_publish(void* gmem_tmap, const void* smem_tmap) {
+    asm volatile("tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;"
+                 :: "l"(gmem_tmap), "r"(smem_u32(smem_tmap)) : "memory");
+}
+
+__device__ __forceinline__ void tmap_acquire(const void* gmem_tmap) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" :: "l"(gmem_tmap) : "memory");
+}
+
 // 1-D bulk copy global -> this CTA's shared memory, completion counted in bytes
 // on an mbarrier.  No multicast (plain per-CTA copy).
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
@@ -143,6 +193,17 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+
+// Atomic add with release semantics at GPU scope: orders this thread's
+// earlier writes (and those ordered before them by a warp or CTA barrier)
+// before the increment, without a separate full fence.
+__device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 // Spin (bounded) until *ctr >= target.  Returns false on timeout.
 __device__ __forceinline__ bool wait_counter(const uint32_t* ctr, uint32_t target, uint32_t* status) {

@@ -7,22 +7,36 @@
 //   -> fp16; down accumulate fp32; output Hadamard + svh fp32; weighted sum
 //   over top-k slots in slot order, fp32; one cast to the output dtype.
 //
-// Structure (B200 design, not the reference's): every CTA builds the same
+// Structure (B200 design, not the reference's).  Every CTA builds the same
 // route plan in shared memory (groups = experts in ascending id, pairs =
-// unique (expert, row)).  Work is a flat ticket space of units:
-//   phase A  (group, 128-col block j of inter, gate|up, k-chunk s of hidden)
-//   phase B  (group, 128-col block c of hidden, k-chunk s of inter)
-// all phase-A tickets before all phase-B tickets.  Partials go to scratch;
-// the last unit of (group, j) finishes gate+up block j and writes the
-// down-input block (SwiGLU + suh + Hadamard) -- the last unit of (group, c)
-// finishes down block c -- the last group to finish block c does the
-// fixed-order gather of that block.  Phase-B units wait (bounded) on a
-// per-(group, chunk) counter.  Every ticket comes from one global counter, so
-// when a CTA holds a phase-B ticket every phase-A ticket has already been
-// claimed by a running CTA; a CTA works its tickets in claim order and
-// phase-A units never wait, so each wait is on work that is in progress and
-// progress needs no co-residency and no grid barrier.
+// unique (expert, row), a group's pairs contiguous).  Then:
+//   P  (consumer warps, at start; items claimed per warp from a counter):
+//      (group, gate|up, 128-block of hidden): x -> fp16, * suh, Hadamard ->
+//      fp16, written to scratch already in MMA B-fragment order;
+//   A  units (group, 128-col block of I, gate|up, k-chunk of hidden);
+//   B  units (group, 128-col block of hidden, k-chunk of I);
+// A and B units come from one global ticket counter, all A before all B.
+// CTA roles: warp 8 (producer) claims a unit, publishes its descriptor, points
+// a tensor map at the expert's matrix, waits (bounded) until the unit's input
+// fragments are ready and streams every stage -- SK k-slices of the unit's 8
+// weight tiles (one 3-D TMA box) plus the matching B fragments (one bulk copy)
+// -- into a shared-memory ring.  Warps 0-7 (consumers) decode n-tile w of
+// each k-slice in registers and run the MMAs, then drop their fp32 partial
+// into a shared-memory tile.  Warp 9 (epilogue) stores the tile, bumps the
+// block's completion counter and, when it completes a block, runs the block
+// epilogue (A: sum the partials, out-Hadamard * svh for gate and up, SwiGLU,
+// down suh + Hadamard -> down-input fragments; B: sum, out-H * svh; the last
+// group to finish a hidden block gathers it in slot order).  The consumers
+// never meet a CTA-wide barrier or a global fence.
+// Waits only point backwards (A on P, B on A), every P item and every unit
+// is claimed by a running warp or CTA and P / A work never waits on later
+// work, so progress needs no co-residency and no grid barrier.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "engine.cuh"
 #include "host.hpp"
@@ -33,19 +47,94 @@ constexpr int kMoeMaxRows = 32;      // row bitmask is one 32-bit word
 constexpr int kMoeMaxSlots = 256;    // m * topk
 constexpr int kMoeMaxExperts = 1024;
 constexpr int kMoeMaxTopk = 16;
-constexpr int kMoeKmax = 4;          // ring slot sized for K <= 4
+constexpr int kMoeKmax = 4;          // weight part of a ring stage sized for K <= 4
 constexpr int kMoeMaxHidden = 8192;
 constexpr int kMoeMaxInter = 4096;
-// Counter strides (per group) inside the control region.
-constexpr int kStrideA = kMoeMaxInter / 128;    // cntA[g][j]
-constexpr int kStrideR = kMoeMaxInter / 128;    // readyB[g][s]
-constexpr int kStrideB = kMoeMaxHidden / 128;   // cntB[g][c]
+constexpr int kMoeSK = 8;                                 // k-slices per ring stage
+constexpr int kMoeWBytes = kMoeSK * 8 * 32 * kMoeKmax;    // weight part of a stage (8 KB)
+constexpr int kMoeRingBytes = 98304;                      // ring + partial tiles per CTA
+constexpr int kMoeDQ = 4;                                 // descriptor queue depth
+constexpr int kMoeMaxNka = 8;                             // hidden k-chunks
+constexpr int kMoeMaxNkb = 4;                             // intermediate k-chunks
+constexpr int kNBImax = kMoeMaxInter / 128;
+constexpr int kNBHmax = kMoeMaxHidden / 128;
+// CTA roles: warps 0-7 consume (decode + MMA), warp 8 produces (tickets,
+// stage copies), warp 9 stores partials and runs the block epilogues.
+constexpr int kMoeConsumerWarps = 8;
+constexpr int kMoeProducerWarp = 8;
+constexpr int kMoeEpilogueWarp = 9;
+constexpr int kMoeThreads = 320;
+// Control region (uint32 words).  ctrl[0] unit ticket, [1] retired CTAs,
+// [2] status word, [3] P-item counter.  Then the per-group counters.
 constexpr int kCtrlWords = 16;
-constexpr int64_t kMoeCtrlNeeded =
-    4LL * (kCtrlWords + (int64_t) kMoeMaxSlots * (kStrideA + kStrideR + kStrideB) + kStrideB);
-static_assert(kMoeCtrlNeeded <= EXL3_MOE_CTRL_BYTES, "control region too small");
+constexpr int kOffCntA = kCtrlWords;                                  // [group][I block]
+constexpr int kOffReadyP = kOffCntA + kMoeMaxSlots * kNBImax;          // [group][2][hidden chunk]
+constexpr int kOffReadyB = kOffReadyP + kMoeMaxSlots * 2 * kMoeMaxNka; // [group][I chunk]
+constexpr int kOffCntB = kOffReadyB + kMoeMaxSlots * kMoeMaxNkb;       // [group][hidden block]
+constexpr int kOffCntG = kOffCntB + kMoeMaxSlots * kNBHmax;            // [hidden block]
+constexpr int kCtrlEnd = kOffCntG + kNBHmax;
+static_assert(4 * kCtrlEnd <= EXL3_MOE_CTRL_BYTES, "control region too small");
+
+// ------------------------------------------------------------------ phase clock
+// Compile-gated phase timers (-DEXL3_PHASE_CLOCK; the B200 counterpart of the
+// reference's LNA2_PHASE_CLOCK, recipe-lna/lna2/lna_moe_ticket.cu:62-64,280-290).
+// Each warp accumulates clock64 cycles per phase in registers and lane 0 adds
+// them into g_phase when the warp retires; exl3_phase_clock_read copies them
+// out.  Release builds compile all of it away.
+#ifdef EXL3_PHASE_CLOCK
+enum {
+    PH_P = 0,          // consumer: input-transform items
+    PH_DESC,           // consumer: waiting for a unit descriptor
+    PH_DATA,           // consumer: waiting for stage data (inside the unit loop)
+    PH_UNIT,           // consumer: unit loop incl. data waits
+    PH_PARTIAL,        // consumer: partial tile write
+    PH_FIN_A,          // epilogue: phase-A block epilogue
+    PH_FIN_B,          // epilogue: phase-B block epilogue + gather
+    PH_PROD_DESC,      // producer: ticket + descriptor publish
+    PH_PROD_DEP,       // producer: tensor map + waiting for input fragments
+    PH_PROD_SLOT,      // producer: waiting for ring slots
+    PH_PROD_ISSUE,     // producer: issuing copies
+    PH_EPI_DESC,       // epilogue: waiting for a descriptor
+    PH_EPI_WAIT,       // epilogue: waiting for a partial tile
+    PH_EPI_STORE,      // epilogue: partial store + completion counter
+    PH_UNITS,          // count of units consumed (per warp)
+    PH_FINS_A,         // count of phase-A epilogues
+    PH_FINS_B,         // count of phase-B epilogues
+    PH_TOTAL,          // cycles from kernel start to warp exit
+    PH_N
+};
+static __device__ unsigned long long g_phase[PH_N];
+#define PHASE_DECL unsigned long long ph_[PH_N] = {}; unsigned long long ph_t_ = clock64(); const unsigned long long ph_start_ = ph_t_;
+#define PHASE_MARK(c) do { const unsigned long long n_ = clock64(); ph_[c] += n_ - ph_t_; ph_t_ = n_; } while (0)
+#define PHASE_COUNT(c) (ph_[c] += 1)
+#define PHASE_FLUSH(lane) do { ph_[PH_TOTAL] = clock64() - ph_start_; if ((lane) == 0) for (int i_ = 0; i_ < PH_N; ++i_) atomicAdd(&g_phase[i_], ph_[i_]); } while (0)
+#define PH_PARAM , unsigned long long& ph_wait
+#define PH_ARG , ph_[PH_DATA]
+#define PH_FWD , ph_wait
+#else
+#define PHASE_DECL
+#define PHASE_MARK(c)
+#define PHASE_COUNT(c)
+#define PHASE_FLUSH(lane)
+#define PH_PARAM
+#define PH_ARG
+#define PH_FWD
+#endif
+
+// Tensor maps: one 3-D map per (projection kind, K) describes an expert
+// matrix as [k/16 slices][n/16 tiles][16K u16 words]; a box is one ring
+// stage (SK slices x 8 tiles).  The host encodes them once per (hidden,
+// intermediate) with a placeholder address; each unit's producer copies the
+// template to shared memory, replaces the address with its expert's matrix
+// and publishes it to a per-CTA global slot.  A slot is rewritten only after
+// every copy issued through it has landed: slots are used round robin and
+// kMoeTmapSlots exceeds the ring depth (<= 8 stages, >= 1 stage per unit).
+constexpr int kMoeTmapSlots = 9;
+constexpr int kMoeMaxGrid = 512;
 
 struct MoeParams {
+    CUtensorMap tmpl[8];        // [kind (0 gate/up, 1 down)][K - 1]
+    CUtensorMap* tmaps;         // [grid][kMoeTmapSlots] per-CTA working maps
     const void* x;
     void* out;
     const int64_t* tab[9];      // gate t/su/sv, up t/su/sv, down t/su/sv
@@ -57,21 +146,13 @@ struct MoeParams {
     float limit;
     int kca, nka;               // gate/up k-chunk over H
     int kcb, nkb;               // down k-chunk over I
-    uint32_t* ctrl;             // [0] ticket [1] retire [2] status
-    uint32_t* cntA;
-    uint32_t* readyB;
-    uint32_t* cntB;
-    uint32_t* cntG;
+    int slot_bytes, ns;         // ring: ns stages of slot_bytes (weights, then B fragments)
+    uint32_t* ctrl;
     float* partA;               // [pairs][2][nka][I]
-    __half* act;                // [pairs][I]
-    float* partB;               // [pairs][nkb][H]
+    uint32_t* xg;               // input fragments: per pair 2 * (H/16) row-slices of 16*FW bytes
+    uint32_t* ag;               // down-input fragments: per pair (I/16) row-slices
+    float* partB;               // [pairs][nkb][H] (== downc when nkb == 1)
     float* downc;               // [pairs][H]
-};
-
-struct MoeCfg {
-    static constexpr int SK = stage_slices(kMoeKmax);
-    static constexpr int STAGE = SK * 8 * TileFmt<kMoeKmax>::BYTES;
-    static constexpr int NS = 49152 / STAGE;
 };
 
 struct MoePlan {
@@ -85,29 +166,16 @@ struct MoePlan {
     int G, P;
 };
 
-struct alignas(128) MoeSmem {
-    uint8_t ring[MoeCfg::NS][MoeCfg::STAGE];
-    uint4 bfrag[kActBytes / 16];
-    float cbuf[kMaxRows * kCols];
-    MoePlan plan;
-    uint64_t full[MoeCfg::NS];
-    uint64_t empty[MoeCfg::NS];
-    uint64_t dqf[kDQ];
-    uint64_t dqe[kDQ];
-    int desc[kDQ][6];                 // kind, g, mat, blk, s, K
-    int rows[kMaxRows];
-    int flag;
-};
-
 // Route plan, identical in every CTA (recipe-lna/lna2/lna_moe_ticket.cu:167-214
 // restated): per-expert row mask, exclusive scans over experts -> group id and
 // first pair, slot -> pair via popcount.  Uses the 256 consumer threads.
 __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
-    const bool worker = tid < kConsumerThreads;
-    for (int e = tid; e < p.E; e += kThreads) P.emask[e] = 0u;
+    const bool worker = tid < kConsumerThreads;      // 256 threads own 4 experts each
+    const int nthr = (int) blockDim.x;
+    for (int e = tid; e < p.E; e += nthr) P.emask[e] = 0u;
     __syncthreads();
     const int nslots = p.m * p.topk;
-    for (int s = tid; s < nslots; s += kThreads) {
+    for (int s = tid; s < nslots; s += nthr) {
         const int id = p.ids[s];
         if (id >= 0 && id < p.E) atomicOr(&P.emask[id], 1u << (s / p.topk));
     }
@@ -157,7 +225,7 @@ __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
         if (tid == kConsumerThreads - 1) { P.G = gh; P.P = gp; }
     }
     __syncthreads();
-    for (int s = tid; s < nslots; s += kThreads) {
+    for (int s = tid; s < nslots; s += nthr) {
         const int id = p.ids[s];
         short sp = -1;
         if (id >= 0 && id < p.E) {
@@ -169,69 +237,292 @@ __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
     __syncthreads();
 }
 
-// Consume one unit's stages for a runtime K / row-block count.
-template <int CB, bool PRECISE, int K>
-__device__ __forceinline__ bool moe_consume_k(MoeSmem& S, uint32_t& it, int nst, int RB, float (&acc)[4][4],
-                                              int cwarp, int lane, uint32_t* status) {
+struct alignas(128) MoeHead {
+    MoePlan plan;
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t dqf[kMoeDQ];
+    uint64_t dqe[kMoeDQ];
+    uint64_t pfull[2];          // partial tile written by the consumer warps
+    uint64_t pempty[2];         // partial tile stored by the epilogue warp
+    int desc[kMoeDQ][8];        // kind, group, mat, block, chunk, K
+    int last_cta;
+    alignas(128) CUtensorMap tmap;   // the producer's tensor map under construction
+};
+constexpr int kMoeHeadBytes = (int) ((sizeof(MoeHead) + 127) / 128 * 128);
+
+// B-fragment words per lane per row-slice: fast arithmetic keeps every
+// activation duplicated into both halves of a word (4 words: k = 2t, 2t+8,
+// 2t+1, 2t+9), the precise path packs pairs (2 words: (2t, 2t+1), (2t+8, 2t+9)).
+template <bool PRECISE> struct Frag { static constexpr int FW = PRECISE ? 2 : 4; };
+
+// Store one transformed activation (row-slice base `rs`, words) at in-slice
+// position kk (0..15) in the fragment layout of Frag<PRECISE>.
+template <bool PRECISE>
+__device__ __forceinline__ void store_frag(uint32_t* rs, int kk, __half h) {
+    const int t = (kk & 7) >> 1;
+    if constexpr (PRECISE) {
+        reinterpret_cast<__half*>(rs)[t * 4 + 2 * (kk >= 8 ? 1 : 0) + (kk & 1)] = h;
+    } else {
+        rs[t * 4 + ((kk & 1) ? 2 : 0) + (kk >= 8 ? 1 : 0)] = dup_half(h);
+    }
+}
+
+// Decode + MMA over `nst` ring stages of one unit; bit width K and row-block
+// count RB are compile-time so the inner loop carries no predicated MMAs.
+template <int K, int RB, int CB, bool PRECISE>
+__device__ __forceinline__ bool moe_consume(const MoeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                            uint32_t& it, int nst, int nrows, float (&acc)[4][4], int cwarp,
+                                            int lane, uint32_t* status PH_PARAM) {
+    using F = TileFmt<K>;
+    constexpr int FW = Frag<PRECISE>::FW;
+    constexpr int ROWW = 8 * F::WORDS;                 // words per k-slice row (8 tiles)
     const LaneGeom<K> geom = lane_geom<K>(lane);
-    // The ring slot is sized for kMoeKmax; a K-bit stage uses its first bytes.
-    auto ring = S.ring;
+    const int t4 = lane & 3, gr = lane >> 2;
+    int boff[RB];
+#pragma unroll
+    for (int rb = 0; rb < RB; ++rb) boff[rb] = min(rb * 8 + gr, nrows - 1) * 4 * FW + t4 * FW;
+    const int bstride = nrows * 4 * FW;                 // words per row-slice block of the unit
+    for (int st = 0; st < nst; ++st) {
+        const int slot = (int) (it % (uint32_t) p.ns);
+#ifdef EXL3_PHASE_CLOCK
+        const unsigned long long w0_ = clock64();
+#endif
+        if (!mbar_wait_lanes(&full[slot], (it / (uint32_t) p.ns) & 1u, status)) return false;
+#ifdef EXL3_PHASE_CLOCK
+        ph_wait += clock64() - w0_;
+#endif
+        const uint32_t* base = reinterpret_cast<const uint32_t*>(ring + (size_t) slot * p.slot_bytes);
+        const uint32_t* phi[F::NG];
+        const uint32_t* plo[F::NG];
+#pragma unroll
+        for (int h = 0; h < F::NG; ++h) {
+            phi[h] = base + cwarp * F::WORDS + geom.ihi[h];
+            plo[h] = base + cwarp * F::WORDS + geom.ilo[h];
+        }
+        const uint32_t* bf = base + kMoeWBytes / 4;
+#pragma unroll
+        for (int i = 0; i < kMoeSK; ++i) {
+            uint32_t whi[F::NG], wlo[F::NG];
+#pragma unroll
+            for (int h = 0; h < F::NG; ++h) {
+                whi[h] = phi[h][i * ROWW];
+                wlo[h] = plo[h][i * ROWW];
+            }
+            uint32_t w[8], x[8];
+            tile_windows_w<K>(whi, wlo, geom, w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[j] = codebook_pair<CB>(w[j]);
+            const uint32_t* bs = bf + i * bstride;
+#pragma unroll
+            for (int rb = 0; rb < RB; ++rb) {
+                if constexpr (PRECISE) {
+                    mma_tile_precise(acc[rb], x, *reinterpret_cast<const uint2*>(bs + boff[rb]));
+                } else {
+                    mma_tile(acc[rb], x, *reinterpret_cast<const uint4*>(bs + boff[rb]));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        ++it;
+    }
+    return true;
+}
+
+template <int K, int CB, bool PRECISE>
+__device__ __forceinline__ bool moe_consume_rb(int RB, const MoeParams& p, uint8_t* ring, uint64_t* full,
+                                               uint64_t* empty, uint32_t& it, int nst, int nrows, float (&acc)[4][4],
+                                               int cwarp, int lane, uint32_t* status PH_PARAM) {
     switch (RB) {
-        case 1: return consume_stages<K, CB, 1, MoeCfg::NS, MoeCfg::STAGE, MoeCfg::SK, PRECISE>(ring, S.full, S.empty, it, nst, 0, S.bfrag, acc, geom, cwarp, lane, status);
-        case 2: return consume_stages<K, CB, 2, MoeCfg::NS, MoeCfg::STAGE, MoeCfg::SK, PRECISE>(ring, S.full, S.empty, it, nst, 0, S.bfrag, acc, geom, cwarp, lane, status);
-        case 3: return consume_stages<K, CB, 3, MoeCfg::NS, MoeCfg::STAGE, MoeCfg::SK, PRECISE>(ring, S.full, S.empty, it, nst, 0, S.bfrag, acc, geom, cwarp, lane, status);
-        default: return consume_stages<K, CB, 4, MoeCfg::NS, MoeCfg::STAGE, MoeCfg::SK, PRECISE>(ring, S.full, S.empty, it, nst, 0, S.bfrag, acc, geom, cwarp, lane, status);
+        case 1: return moe_consume<K, 1, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        case 2: return moe_consume<K, 2, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        case 3: return moe_consume<K, 3, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        default: return moe_consume<K, 4, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
     }
 }
 
 template <int CB, bool PRECISE>
-__device__ __forceinline__ bool moe_consume(MoeSmem& S, uint32_t& it, int nst, int K, int RB, float (&acc)[4][4],
-                                            int cwarp, int lane, uint32_t* status) {
+__device__ __forceinline__ bool moe_consume_any(int K, int RB, const MoeParams& p, uint8_t* ring, uint64_t* full,
+                                                uint64_t* empty, uint32_t& it, int nst, int nrows, float (&acc)[4][4],
+                                                int cwarp, int lane, uint32_t* status PH_PARAM) {
     switch (K) {
-        case 1: return moe_consume_k<CB, PRECISE, 1>(S, it, nst, RB, acc, cwarp, lane, status);
-        case 2: return moe_consume_k<CB, PRECISE, 2>(S, it, nst, RB, acc, cwarp, lane, status);
-        case 3: return moe_consume_k<CB, PRECISE, 3>(S, it, nst, RB, acc, cwarp, lane, status);
-        default: return moe_consume_k<CB, PRECISE, 4>(S, it, nst, RB, acc, cwarp, lane, status);
+        case 1: return moe_consume_rb<1, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        case 2: return moe_consume_rb<2, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        case 3: return moe_consume_rb<3, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        default: return moe_consume_rb<4, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
     }
 }
 
-__device__ __forceinline__ int unit_count_A(const MoeParams& p, int G) { return G * (p.I / kCols) * 2 * p.nka; }
-__device__ __forceinline__ int unit_count_B(const MoeParams& p, int G) { return G * (p.H / kCols) * p.nkb; }
+// Phase P: one warp transforms hidden block kb of every row of group g for
+// projection mat (0 gate, 1 up): fp16(x) * suh in fp16, 128-point Hadamard in
+// fp32, * 1/sqrt(128) -> fp16 (recipe-lna/lna2/lna_moe_ticket.cu:119-144),
+// written as B fragments.
+template <bool PRECISE>
+__device__ void moe_input_item(const MoeParams& p, const MoePlan& P, int g, int mat, int kb, int lane) {
+    constexpr int FW = Frag<PRECISE>::FW;
+    const int e = P.gexp[g];
+    uint32_t gm = P.gmask[g];
+    const int nrows = __popc(gm), pair0 = P.gpair[g];
+    const int HS = p.H / 16;
+    const __half* suh = reinterpret_cast<const __half*>(p.tab[mat ? 4 : 1][e]);
+    uint32_t* gbase = p.xg + (size_t) pair0 * 2 * HS * 4 * FW;
+    const int k0 = kb * 128 + lane * 4;
+    for (int ri = 0; ri < nrows; ++ri) {
+        const int row = __ffs((int) gm) - 1;
+        gm &= gm - 1u;
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __half a = load_act_half(p.x, p.x_dtype, (int64_t) row * p.H + k0 + q);
+            v[q] = __half2float(__hmul(a, suh[k0 + q]));
+        }
+        wht128_warp(v, lane);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int kl = lane * 4 + q;
+            const int ks = kb * 8 + (kl >> 4);
+            uint32_t* rs = gbase + ((size_t) (mat * HS + ks) * nrows + ri) * 4 * FW;
+            store_frag<PRECISE>(rs, kl & 15, __float2half_rn(v[q] * kHadNorm));
+        }
+    }
+}
+
+// Phase-A epilogue of (group g, I block blk), by one warp: sum the gate and up
+// partials in fixed order, output transform, SwiGLU (clamp, then SiLU), down
+// suh + Hadamard -> fp16 down-input fragments (lna_moe_ticket.cu:329-359).
+template <bool PRECISE>
+__device__ void moe_finish_a(const MoeParams& p, const MoePlan& P, int g, int blk, int lane) {
+    constexpr int FW = Frag<PRECISE>::FW;
+    const int e = P.gexp[g];
+    const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
+    const int IS = p.I / 16;
+    const __half* gsv = reinterpret_cast<const __half*>(p.tab[2][e]) + blk * kCols;
+    const __half* usv = reinterpret_cast<const __half*>(p.tab[5][e]) + blk * kCols;
+    const __half* dsu = reinterpret_cast<const __half*>(p.tab[7][e]) + blk * kCols;
+    uint32_t* abase = p.ag + (size_t) pair0 * IS * 4 * FW;
+    for (int ri = 0; ri < nrows; ++ri) {
+        const int64_t pr = pair0 + ri;
+        float gv[4] = {0.f, 0.f, 0.f, 0.f}, uv[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c2 = 0; c2 < p.nka; ++c2) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(
+                p.partA + ((pr * 2 + 0) * p.nka + c2) * p.I + blk * kCols + lane * 4));
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(
+                p.partA + ((pr * 2 + 1) * p.nka + c2) * p.I + blk * kCols + lane * 4));
+            gv[0] += a.x; gv[1] += a.y; gv[2] += a.z; gv[3] += a.w;
+            uv[0] += b.x; uv[1] += b.y; uv[2] += b.z; uv[3] += b.w;
+        }
+        out_transform(gv, gsv, lane);
+        out_transform(uv, usv, lane);
+        float dv[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float gg = gv[q], uu = uv[q];
+            if (gg > p.limit) gg = p.limit;
+            if (uu < -p.limit) uu = -p.limit;
+            if (uu > p.limit) uu = p.limit;
+            const __half a = __float2half_rn((gg / (1.0f + __expf(-gg))) * uu);
+            dv[q] = __half2float(__hmul(a, dsu[lane * 4 + q]));
+        }
+        wht128_warp(dv, lane);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int kl = lane * 4 + q;
+            const int ks = blk * 8 + (kl >> 4);
+            uint32_t* rs = abase + ((size_t) ks * nrows + ri) * 4 * FW;
+            store_frag<PRECISE>(rs, kl & 15, __float2half_rn(dv[q] * kHadNorm));
+        }
+    }
+}
+
+// Phase-B epilogue of (group g, hidden block blk), by one warp: sum the down
+// partials, output transform (lna_moe_ticket.cu:368-378); the last group to
+// finish block blk gathers it for every row in slot order (:409-428).
+__device__ void moe_finish_b(const MoeParams& p, const MoePlan& P, int g, int blk, int lane, uint32_t* cntG) {
+    const int e = P.gexp[g];
+    const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
+    const __half* dsv = reinterpret_cast<const __half*>(p.tab[8][e]) + blk * kCols;
+    for (int ri = 0; ri < nrows; ++ri) {
+        const int64_t pr = pair0 + ri;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c2 = 0; c2 < p.nkb; ++c2) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(
+                p.partB + (pr * p.nkb + c2) * p.H + blk * kCols + lane * 4));
+            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        }
+        out_transform(v, dsv, lane);
+        __stcg(reinterpret_cast<float4*>(p.downc + pr * p.H + blk * kCols + lane * 4),
+               make_float4(v[0], v[1], v[2], v[3]));
+    }
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+        const uint32_t old = atom_add_release_gpu(&cntG[blk], 1u);
+        last = old == (uint32_t) (P.G - 1);
+        if (last) {
+            atomicExch(&cntG[blk], 0u);
+            fence_acq_rel_gpu();
+        }
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    for (int r = 0; r < p.m; ++r) {
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < p.topk; ++k) {
+            const int pr = P.slotpair[r * p.topk + k];
+            if (pr >= 0) {
+                const float wv = p.weights[r * p.topk + k];
+                const float4 d = __ldcg(reinterpret_cast<const float4*>(
+                    p.downc + (int64_t) pr * p.H + blk * kCols + lane * 4));
+                s[0] += wv * d.x; s[1] += wv * d.y; s[2] += wv * d.z; s[3] += wv * d.w;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
+    }
+}
 
 template <int CB, bool PRECISE>
-__global__ void __launch_bounds__(kThreads, 2) moe_kernel(MoeParams p) {
+__global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_constant__ MoeParams p) {
+    constexpr int FW = Frag<PRECISE>::FW;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    MoeSmem& S = *reinterpret_cast<MoeSmem*>(smem_raw);
+    MoeHead& S = *reinterpret_cast<MoeHead*>(smem_raw);
+    uint8_t* ring = smem_raw + kMoeHeadBytes;
+    float* ptile = reinterpret_cast<float*>(ring + (size_t) p.ns * p.slot_bytes);   // [2][m][128]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t* status = p.ctrl + 2;
+    uint32_t* cntA = p.ctrl + kOffCntA;
+    uint32_t* readyP = p.ctrl + kOffReadyP;
+    uint32_t* readyB = p.ctrl + kOffReadyB;
+    uint32_t* cntB = p.ctrl + kOffCntB;
+    uint32_t* cntG = p.ctrl + kOffCntG;
 
     if (tid == 0) {
-        for (int s = 0; s < MoeCfg::NS; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kConsumerWarps); }
-        for (int s = 0; s < kDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], 1); }
+        for (int s = 0; s < p.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kMoeConsumerWarps); }
+        for (int s = 0; s < kMoeDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], kMoeConsumerWarps + 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&S.pfull[s], kMoeConsumerWarps); mbar_init(&S.pempty[s], 1); }
         fence_barrier_init();
     }
-    build_plan(S.plan, p, tid);
+    build_plan(S.plan, p, tid);     // ends with __syncthreads (also publishes the barrier init)
     const MoePlan& P = S.plan;
     const int G = P.G;
     const int NBI = p.I / kCols, NBH = p.H / kCols;
-    const int UA = unit_count_A(p, G);
-    const int total = UA + unit_count_B(p, G);
+    const int UA = G * NBI * 2 * p.nka;
+    const int total = UA + G * NBH * p.nkb;
 
     if (G == 0 && blockIdx.x == 0) {
         // No valid route: the layer output is zero.
-        for (int i = tid; i < p.m * p.H; i += kThreads) store_out(p.out, p.out_dtype, i, 0.f);
+        for (int i = tid; i < p.m * p.H; i += kMoeThreads) store_out(p.out, p.out_dtype, i, 0.f);
     }
 
-    if (warp == kProducerWarp) {
-        // ---------------------------------------------------------- producer
+    if (warp == kMoeProducerWarp) {
+        // ------------------------------------------------------------ producer
+        PHASE_DECL
         int ticket = claim_ticket(&p.ctrl[0], lane);
-        uint32_t it = 0, du = 0;
+        uint32_t it = 0, du = 0, units = 0;
         bool ok = true;
         while (ok) {
             int d[6] = {-1, 0, 0, 0, 0, 0};
-            const uint8_t* src = nullptr;
-            int64_t rowstride = 0;
-            int nst = 0, K = 0;
             if (ticket < total) {
                 int g, mat = 0, blk, s, kind;
                 if (ticket < UA) {
@@ -252,29 +543,13 @@ __global__ void __launch_bounds__(kThreads, 2) moe_kernel(MoeParams p) {
                     blk = r / p.nkb;
                     s = r % p.nkb;
                 }
-                const int e = P.gexp[g];
-                K = p.ktab ? p.ktab[e] : p.kuni;
+                int K = p.ktab ? p.ktab[P.gexp[g]] : p.kuni;
+                if (K < 1 || K > kMoeKmax) K = 0;
                 d[0] = kind; d[1] = g; d[2] = mat; d[3] = blk; d[4] = s; d[5] = K;
-                if (K >= 1 && K <= kMoeKmax) {
-                    const int tb = 32 * K;
-                    if (kind == 0) {
-                        src = reinterpret_cast<const uint8_t*>(p.tab[mat ? 3 : 0][e]);
-                        rowstride = (int64_t) (p.I / 16) * tb;
-                        src += (int64_t) s * (p.kca / 16) * rowstride + (int64_t) blk * 8 * tb;
-                        nst = p.kca / (16 * MoeCfg::SK);
-                    } else {
-                        src = reinterpret_cast<const uint8_t*>(p.tab[6][e]);
-                        rowstride = (int64_t) (p.H / 16) * tb;
-                        src += (int64_t) s * (p.kcb / 16) * rowstride + (int64_t) blk * 8 * tb;
-                        nst = p.kcb / (16 * MoeCfg::SK);
-                    }
-                } else {
-                    d[5] = 0;   // consumers skip the unit (error recorded)
-                }
             }
             if (lane == 0) {
-                const int slot = du % kDQ;
-                ok = mbar_wait(&S.dqe[slot], ((du / kDQ) + 1u) & 1u, status);
+                const int slot = du % kMoeDQ;
+                ok = mbar_wait(&S.dqe[slot], ((du / kMoeDQ) + 1u) & 1u, status);
                 if (ok) {
 #pragma unroll
                     for (int q = 0; q < 6; ++q) S.desc[slot][q] = d[q];
@@ -283,221 +558,224 @@ __global__ void __launch_bounds__(kThreads, 2) moe_kernel(MoeParams p) {
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             ++du;
+            PHASE_MARK(PH_PROD_DESC);
             if (d[0] < 0 || !ok) break;
             if (d[5] == 0) {
                 if (lane == 0) set_error(status, ERR_BAD_K);
+                ticket = claim_ticket(&p.ctrl[0], lane);
+                continue;
+            }
+            const int kind = d[0], g = d[1], mat = d[2], blk = d[3], s = d[4], K = d[5];
+            const int e = P.gexp[g];
+            const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
+            const int tb = 32 * K;                  // bytes per tile
+            const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.tab[kind == 0 ? (mat ? 3 : 0) : 6][e]);
+            const uint8_t* bsrc;
+            int ks0, nst;
+            const int64_t rsb = (int64_t) nrows * 16 * FW;   // B-fragment bytes per k-slice
+            if (kind == 0) {
+                ks0 = s * (p.kca / 16);
+                bsrc = reinterpret_cast<const uint8_t*>(p.xg) + (int64_t) pair0 * 2 * p.H * FW +
+                       ((int64_t) mat * (p.H / 16) + ks0) * rsb;
+                nst = p.kca / (16 * kMoeSK);
             } else {
-                const int rowbytes = 8 * 32 * K;
-                const bool valid = aligned16_dev(src) && (rowstride & 15) == 0;
-                if (!valid && lane == 0) set_error(status, ERR_MISALIGNED);
-                for (int st = 0; st < nst && ok; ++st)
-                    ok = produce_stage<MoeCfg::NS, MoeCfg::STAGE>(S.ring, S.full, S.empty, it,
-                                                                  src + (int64_t) st * MoeCfg::SK * rowstride,
-                                                                  rowstride, rowbytes, MoeCfg::SK, valid, lane,
-                                                                  status);
+                ks0 = s * (p.kcb / 16);
+                bsrc = reinterpret_cast<const uint8_t*>(p.ag) + (int64_t) pair0 * p.I * FW + (int64_t) ks0 * rsb;
+                nst = p.kcb / (16 * kMoeSK);
+            }
+            const bool valid = aligned16_dev(wbase);
+            if (!valid && lane == 0) set_error(status, ERR_MISALIGNED);
+            // Point this unit's tensor map at the expert's matrix.
+            CUtensorMap* gtm = p.tmaps + (size_t) blockIdx.x * kMoeTmapSlots + (int) (units % kMoeTmapSlots);
+            ++units;
+            if (valid) {
+                const uint4* tsrc = reinterpret_cast<const uint4*>(&p.tmpl[kind * 4 + K - 1]);
+                if (lane < 8) reinterpret_cast<uint4*>(&S.tmap)[lane] = tsrc[lane];
+                __syncwarp();
+                if (lane == 0) tmap_replace_address(&S.tmap, wbase);
+                __syncwarp();
+                tmap_publish(gtm, &S.tmap);
+                if (lane == 0) tmap_acquire(gtm);
+            }
+            // The unit's input fragments must be complete before they are copied.
+            if (lane == 0) {
+                if (kind == 0) wait_counter(&readyP[(g * 2 + mat) * kMoeMaxNka + s], (uint32_t) (p.kca / kCols), status);
+                else wait_counter(&readyB[g * kMoeMaxNkb + s], (uint32_t) (p.kcb / kCols), status);
+                fence_proxy_async_global();
+            }
+            __syncwarp();
+            PHASE_MARK(PH_PROD_DEP);
+            const uint32_t wbytes = (uint32_t) (kMoeSK * 8 * tb);
+            const int bbytes = (int) (kMoeSK * rsb);
+            for (int st = 0; st < nst && ok; ++st) {
+                const int slot = (int) (it % (uint32_t) p.ns);
+                if (lane == 0) {
+                    ok = mbar_wait(&S.empty[slot], ((it / (uint32_t) p.ns) + 1u) & 1u, status);
+                    PHASE_MARK(PH_PROD_SLOT);
+                    if (ok) {
+                        uint8_t* dst = ring + (size_t) slot * p.slot_bytes;
+                        if (valid) {
+                            mbar_arrive_expect_tx(&S.full[slot], wbytes + (uint32_t) bbytes);
+                            tma_load_3d(dst, gtm, 0, blk * 8, ks0 + st * kMoeSK, &S.full[slot]);
+                            bulk_g2s(dst + kMoeWBytes, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
+                        } else {
+                            mbar_arrive(&S.full[slot]);
+                        }
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                ++it;
+                PHASE_MARK(PH_PROD_ISSUE);
             }
             ticket = claim_ticket(&p.ctrl[0], lane);
         }
-        drain_ring<MoeCfg::NS>(S.full, it, lane, status);
-    } else {
-        // ---------------------------------------------------------- consumers
-        const int ctid = tid;
-        uint32_t it = 0, du = 0;
+        // no bulk copy may still be writing shared memory when the CTA retires
+        if (lane == 0) {
+            const uint32_t first = it > (uint32_t) p.ns ? it - (uint32_t) p.ns : 0u;
+            for (uint32_t i = first; i < it; ++i)
+                if (!mbar_wait(&S.full[i % p.ns], (i / p.ns) & 1u, status)) break;
+        }
+        PHASE_FLUSH(lane);
+    } else if (warp == kMoeEpilogueWarp) {
+        // ------------------------------------------------------------ epilogue
+        // Stores each unit's partial tile, counts completions per block and runs
+        // the block epilogues, off the consumers' critical path.
+        PHASE_DECL
+        uint32_t du = 0, uu = 0;
         while (true) {
-            const int slot = du % kDQ;
-            if (!consumers_all(mbar_wait_warp(&S.dqf[slot], (du / kDQ) & 1u, status, lane))) break;
+            const int slot = du % kMoeDQ;
+            if (!mbar_wait_lanes(&S.dqf[slot], (du / kMoeDQ) & 1u, status)) break;
             int d[6];
 #pragma unroll
             for (int q = 0; q < 6; ++q) d[q] = S.desc[slot][q];
-            consumers_sync();
-            if (ctid == 0) mbar_arrive(&S.dqe[slot]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
+            PHASE_MARK(PH_EPI_DESC);
             if (d[0] < 0) break;
             const int kind = d[0], g = d[1], mat = d[2], blk = d[3], s = d[4], K = d[5];
             if (K == 0) continue;
-            const int e = P.gexp[g];
-            const uint32_t gm = P.gmask[g];
-            const int nrows = __popc(gm);
-            const int pair0 = P.gpair[g];
-            const int RB = row_blocks(nrows);
-            if (ctid < kMaxRows) {
-                int r = -1;
-                if (ctid < nrows) {
-                    if (kind == 0) {
-                        // ctid-th set bit of the row mask
-                        uint32_t mk = gm;
-                        for (int q = 0; q < ctid; ++q) mk &= mk - 1u;
-                        r = __ffs((int) mk) - 1;
-                    } else {
-                        r = pair0 + ctid;
-                    }
+            const int ps = (int) (uu & 1u);
+            if (!mbar_wait_lanes(&S.pfull[ps], (uu >> 1) & 1u, status)) break;
+            PHASE_MARK(PH_EPI_WAIT);
+            const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
+            const float* tile = ptile + (size_t) ps * p.m * kCols;
+            for (int r = 0; r < nrows; ++r) {
+                const float4 v = *reinterpret_cast<const float4*>(tile + r * kCols + lane * 4);
+                float* dst = kind == 0
+                    ? p.partA + (((int64_t) (pair0 + r) * 2 + mat) * p.nka + s) * p.I + blk * kCols
+                    : p.partB + ((int64_t) (pair0 + r) * p.nkb + s) * p.H + blk * kCols;
+                __stcg(reinterpret_cast<float4*>(dst + lane * 4), v);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.pempty[ps]);
+            ++uu;
+            int last = 0;
+            if (lane == 0) {
+                uint32_t* cnt = kind == 0 ? &cntA[g * kNBImax + blk] : &cntB[g * kNBHmax + blk];
+                const uint32_t target = kind == 0 ? (uint32_t) (2 * p.nka) : (uint32_t) p.nkb;
+                // release this unit's partial (the whole warp's stores, ordered by
+                // the __syncwarp above)
+                const uint32_t old = atom_add_release_gpu(cnt, 1u);
+                last = old == target - 1u;
+                if (last) {
+                    atomicExch(cnt, 0u);
+                    fence_acq_rel_gpu();   // acquire every unit's partial of the block
                 }
-                S.rows[ctid] = r;
             }
-            if (kind == 1 && ctid == 0) {
-                // down input chunk s of this group must be complete
-                wait_counter(&p.readyB[g * kStrideR + s], (uint32_t) (p.kcb / kCols), status);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            PHASE_MARK(PH_EPI_STORE);
+            if (!last) continue;
+            if (kind == 0) {
+                PHASE_COUNT(PH_FINS_A);
+                moe_finish_a<PRECISE>(p, P, g, blk, lane);
+                __syncwarp();
+                if (lane == 0) {
+                    fence_proxy_async_global();   // release the down-input fragments
+                    atom_add_release_gpu(&readyB[g * kMoeMaxNkb + (blk * kCols) / p.kcb], 1u);
+                }
+                PHASE_MARK(PH_FIN_A);
+            } else {
+                PHASE_COUNT(PH_FINS_B);
+                moe_finish_b(p, P, g, blk, lane, cntG);
+                PHASE_MARK(PH_FIN_B);
             }
-            consumers_sync();
+        }
+        PHASE_FLUSH(lane);
+    } else {
+        // ------------------------------------------------------------ consumers
+        // Phase P: input transforms, claimed one warp at a time.
+        PHASE_DECL
+        const int NKB = p.H / kCols;
+        const int PI = G * 2 * NKB;
+        while (true) {
+            int item = 0;
+            if (lane == 0) item = (int) atomicAdd(&p.ctrl[3], 1u);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            if (item >= PI) break;
+            const int g = item / (2 * NKB);
+            const int r = item % (2 * NKB);
+            const int mat = r / NKB, kb = r % NKB;
+            moe_input_item<PRECISE>(p, P, g, mat, kb, lane);
+            __syncwarp();
+            if (lane == 0) {
+                fence_proxy_async_global();
+                atom_add_release_gpu(&readyP[(g * 2 + mat) * kMoeMaxNka + kb / (p.kca / kCols)], 1u);
+            }
+        }
+        PHASE_MARK(PH_P);
 
-            const int kc = kind == 0 ? p.kca : p.kcb;
-            const int kslices = kc / 16;
-            const int sub0 = (act_slices(RB) / 16) * 16;
-            const int sub = sub0 < kslices ? sub0 : kslices;
+        uint32_t it = 0, du = 0, uu = 0;
+        const int t4 = lane & 3, gr = lane >> 2;
+        while (true) {
+            const int slot = du % kMoeDQ;
+            if (!mbar_wait_lanes(&S.dqf[slot], (du / kMoeDQ) & 1u, status)) break;
+            PHASE_MARK(PH_DESC);
+            int d[6];
+#pragma unroll
+            for (int q = 0; q < 6; ++q) d[q] = S.desc[slot][q];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.dqe[slot]);
+            ++du;
+            if (d[0] < 0) break;
+            const int kind = d[0], g = d[1], K = d[5];
+            if (K == 0) continue;
+            const int nrows = __popc(P.gmask[g]);
+            const int nst = (kind == 0 ? p.kca : p.kcb) / (16 * kMoeSK);
             float acc[4][4];
 #pragma unroll
             for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-            bool ok = true;
-            for (int ks0 = 0; ks0 < kslices && ok; ks0 += sub) {
-                const int nks = min(sub, kslices - ks0);
-                if (ks0 > 0) consumers_sync();
-                if (kind == 0) {
-                    const __half* suh = reinterpret_cast<const __half*>(p.tab[mat ? 4 : 1][e]);
-                    build_bfrag<PRECISE>(S.bfrag, RB, nrows, S.rows, p.x, p.x_dtype, p.H, s * kslices + ks0, nks,
-                                         suh, warp, lane);
-                } else {
-                    build_bfrag<PRECISE>(S.bfrag, RB, nrows, S.rows, p.act, 0, p.I, s * kslices + ks0, nks, nullptr,
-                                         warp, lane);
-                }
-                consumers_sync();
-                ok = consumers_all(moe_consume<CB, PRECISE>(S, it, nks / MoeCfg::SK, K, RB, acc, warp, lane, status));
-            }
-            if (!consumers_all(ok)) break;
-            acc_to_cbuf(S.cbuf, acc, RB, warp, lane);
-            consumers_sync();
-
-            if (kind == 0) {
-                // ---- phase A: partial, then maybe finish gate+up block blk
-                for (int idx = ctid; idx < nrows * kCols; idx += kConsumerThreads) {
-                    const int r = idx / kCols, c = idx % kCols;
-                    p.partA[(((int64_t) (pair0 + r) * 2 + mat) * p.nka + s) * p.I + blk * kCols + c] = S.cbuf[idx];
-                }
-                consumers_sync();
-                if (ctid == 0) {
-                    __threadfence();   // release: covers every consumer's writes (ordered by the barrier)
-                    const uint32_t old = atomicAdd(&p.cntA[g * kStrideA + blk], 1u);
-                    const int last = old == (uint32_t) (2 * p.nka - 1);
-                    if (last) {
-                        atomicExch(&p.cntA[g * kStrideA + blk], 0u);
-                        __threadfence();   // acquire: the other units' partials
-                    }
-                    S.flag = last;
-                }
-                consumers_sync();
-                if (S.flag) {
-                    const __half* gsv = reinterpret_cast<const __half*>(p.tab[2][e]) + blk * kCols;
-                    const __half* usv = reinterpret_cast<const __half*>(p.tab[5][e]) + blk * kCols;
-                    const __half* dsu = reinterpret_cast<const __half*>(p.tab[7][e]) + blk * kCols;
-                    for (int r = warp; r < nrows; r += kConsumerWarps) {
-                        const int64_t pr = pair0 + r;
-                        float gv[4], uv[4];
+            const bool ok = moe_consume_any<CB, PRECISE>(K, row_blocks(nrows), p, ring, S.full, S.empty, it, nst,
+                                                         nrows, acc, warp, lane, status PH_ARG);
+            PHASE_MARK(PH_UNIT);
+            PHASE_COUNT(PH_UNITS);
+            if (!ok) break;
+            // this warp's 16 columns into the partial tile: D fragment (ch gr, row 2t),
+            // (gr, 2t+1), (gr+8, 2t), (gr+8, 2t+1)
+            const int ps = (int) (uu & 1u);
+            if (!mbar_wait_lanes(&S.pempty[ps], ((uu >> 1) + 1u) & 1u, status)) break;
+            float* tile = ptile + (size_t) ps * p.m * kCols;
+            const int col = warp * 16 + gr;
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            float a = 0.f, b = 0.f;
-                            for (int c2 = 0; c2 < p.nka; ++c2) {
-                                a += __ldcg(&p.partA[((pr * 2 + 0) * p.nka + c2) * p.I + blk * kCols + lane * 4 + q]);
-                                b += __ldcg(&p.partA[((pr * 2 + 1) * p.nka + c2) * p.I + blk * kCols + lane * 4 + q]);
-                            }
-                            gv[q] = a;
-                            uv[q] = b;
-                        }
-                        out_transform(gv, gsv, lane);
-                        out_transform(uv, usv, lane);
-                        float dv[4];
+            for (int rb = 0; rb < 4; ++rb) {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            float gg = gv[q], uu = uv[q];
-                            if (gg > p.limit) gg = p.limit;
-                            if (uu < -p.limit) uu = -p.limit;
-                            if (uu > p.limit) uu = p.limit;
-                            const __half a = __float2half_rn((gg / (1.0f + __expf(-gg))) * uu);
-                            dv[q] = __half2float(__hmul(a, dsu[lane * 4 + q]));
-                        }
-                        wht128_warp(dv, lane);
-                        __half* dst = p.act + pr * p.I + blk * kCols + lane * 4;
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) dst[q] = __float2half_rn(dv[q] * kHadNorm);
-                    }
-                    consumers_sync();
-                    if (ctid == 0) {
-                        __threadfence();   // release the down-input block
-                        atomicAdd(&p.readyB[g * kStrideR + (blk * kCols) / p.kcb], 1u);
-                    }
-                }
-            } else {
-                // ---- phase B: partial, then maybe finish down block blk
-                bool fin = true;
-                if (p.nkb > 1) {
-                    for (int idx = ctid; idx < nrows * kCols; idx += kConsumerThreads) {
-                        const int r = idx / kCols, c = idx % kCols;
-                        p.partB[((int64_t) (pair0 + r) * p.nkb + s) * p.H + blk * kCols + c] = S.cbuf[idx];
-                    }
-                    consumers_sync();
-                    if (ctid == 0) {
-                        __threadfence();
-                        const uint32_t old = atomicAdd(&p.cntB[g * kStrideB + blk], 1u);
-                        const int last = old == (uint32_t) (p.nkb - 1);
-                        if (last) {
-                            atomicExch(&p.cntB[g * kStrideB + blk], 0u);
-                            __threadfence();
-                        }
-                        S.flag = last;
-                    }
-                    consumers_sync();
-                    fin = S.flag != 0;
-                    if (fin) {
-                        for (int idx = ctid; idx < nrows * kCols; idx += kConsumerThreads) {
-                            const int r = idx / kCols, c = idx % kCols;
-                            float v = 0.f;
-                            for (int c2 = 0; c2 < p.nkb; ++c2)
-                                v += __ldcg(&p.partB[((int64_t) (pair0 + r) * p.nkb + c2) * p.H + blk * kCols + c]);
-                            S.cbuf[idx] = v;
-                        }
-                        consumers_sync();
-                    }
-                }
-                if (fin) {
-                    const __half* dsv = reinterpret_cast<const __half*>(p.tab[8][e]) + blk * kCols;
-                    for (int r = warp; r < nrows; r += kConsumerWarps) {
-                        float v[4];
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) v[q] = S.cbuf[r * kCols + lane * 4 + q];
-                        out_transform(v, dsv, lane);
-                        float4 o = make_float4(v[0], v[1], v[2], v[3]);
-                        __stcg(reinterpret_cast<float4*>(p.downc + (int64_t) (pair0 + r) * p.H + blk * kCols + lane * 4), o);
-                    }
-                    consumers_sync();
-                    if (ctid == 0) {
-                        __threadfence();
-                        const uint32_t old = atomicAdd(&p.cntG[blk], 1u);
-                        const int last = old == (uint32_t) (G - 1);
-                        if (last) {
-                            atomicExch(&p.cntG[blk], 0u);
-                            __threadfence();
-                        }
-                        S.flag = last;
-                    }
-                    consumers_sync();
-                    if (S.flag) {
-                        // fixed-order gather of column block blk for every row
-                        for (int idx = ctid; idx < p.m * kCols; idx += kConsumerThreads) {
-                            const int r = idx / kCols, c = idx % kCols;
-                            float sum = 0.f;
-                            for (int k = 0; k < p.topk; ++k) {
-                                const int pr = P.slotpair[r * p.topk + k];
-                                if (pr >= 0)
-                                    sum += p.weights[r * p.topk + k] *
-                                           __ldcg(&p.downc[(int64_t) pr * p.H + blk * kCols + c]);
-                            }
-                            store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + c, sum);
-                        }
+                for (int h = 0; h < 2; ++h) {
+                    const int r = rb * 8 + 2 * t4 + h;
+                    if (r < nrows) {
+                        tile[r * kCols + col] = acc[rb][h];
+                        tile[r * kCols + col + 8] = acc[rb][2 + h];
                     }
                 }
             }
-            consumers_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.pfull[ps]);
+            ++uu;
+            PHASE_MARK(PH_PARTIAL);
         }
+        PHASE_FLUSH(lane);
     }
 
     // Retire: the last CTA out restores the control region for the next launch.
@@ -505,14 +783,16 @@ __global__ void __launch_bounds__(kThreads, 2) moe_kernel(MoeParams p) {
     if (tid == 0) {
         __threadfence();
         const uint32_t old = atomicAdd(&p.ctrl[1], 1u);
-        S.flag = old == gridDim.x - 1;
+        S.last_cta = old == gridDim.x - 1;
     }
     __syncthreads();
-    if (S.flag) {
+    if (S.last_cta) {
         __threadfence();
-        for (int i = tid; i < G * kStrideR; i += kThreads) p.readyB[i] = 0u;
+        for (int i = tid; i < G * 2 * kMoeMaxNka; i += kMoeThreads) readyP[i] = 0u;
+        for (int i = tid; i < G * kMoeMaxNkb; i += kMoeThreads) readyB[i] = 0u;
         if (tid == 0) {
             atomicExch(&p.ctrl[0], 0u);
+            atomicExch(&p.ctrl[3], 0u);
             atomicExch(&p.ctrl[1], 0u);
         }
     }
@@ -521,31 +801,112 @@ __global__ void __launch_bounds__(kThreads, 2) moe_kernel(MoeParams p) {
 // ------------------------------------------------------------------ host side
 namespace {
 
+// Number of k-chunks of a dimension of `n` elements: the smallest count
+// >= ceil(n / 1024) that splits it into whole 128-element blocks, at most
+// `cap` (the largest such divisor otherwise).
+int chunks_for(int64_t n, int cap) {
+    const int64_t blocks = n / 128;
+    const int lo = (int) ((n + 1023) / 1024);
+    for (int c = lo; c <= cap; ++c)
+        if (blocks % c == 0) return c;
+    for (int c = cap; c >= 1; --c)
+        if (blocks % c == 0) return c;
+    return 1;
+}
+
 struct MoeGeom {
     int kca, nka, kcb, nkb;
     int64_t pairs;
-    int64_t off_partA, off_act, off_partB, off_downc, total;
+    int64_t off_tmaps, off_partA, off_xg, off_ag, off_partB, off_downc, total;
 };
 
+// Scratch geometry (fragments sized for the fast path's 4 words per lane,
+// which the precise path's 2 words also fit).
 MoeGeom moe_geom(int64_t m, int64_t topk, int64_t H, int64_t I) {
     MoeGeom g{};
-    g.kca = H >= 1024 && H % 1024 == 0 ? 1024 : (H % 512 == 0 ? 512 : (H % 256 == 0 ? 256 : 128));
-    g.nka = (int) (H / g.kca);
-    g.kcb = I >= 1024 && I % 1024 == 0 ? 1024 : (I % 512 == 0 ? 512 : (I % 256 == 0 ? 256 : 128));
-    if (g.kcb > I) g.kcb = (int) I;
-    g.nkb = (int) (I / g.kcb);
+    g.nka = chunks_for(H, kMoeMaxNka);
+    g.kca = (int) (H / g.nka);
+    g.nkb = chunks_for(I, kMoeMaxNkb);
+    g.kcb = (int) (I / g.nkb);
     g.pairs = m * topk;
     int64_t off = EXL3_MOE_CTRL_BYTES;
+    g.off_tmaps = off;                               // per-CTA tensor-map slots
+    off = align_up(off + (int64_t) kMoeMaxGrid * kMoeTmapSlots * (int64_t) sizeof(CUtensorMap), 256);
     g.off_partA = off;
     off = align_up(off + g.pairs * 2 * g.nka * I * 4, 256);
-    g.off_act = off;
-    off = align_up(off + g.pairs * I * 2, 256);
-    g.off_partB = off;
+    g.off_xg = off;                                  // per pair: 2 projections x H x FW bytes
+    off = align_up(off + g.pairs * 2 * H * 4, 256);
+    g.off_ag = off;                                  // per pair: I x FW bytes
+    off = align_up(off + g.pairs * I * 4, 256);
+    g.off_partB = off;                               // with one I chunk the partials alias downc
     off = align_up(off + (g.nkb > 1 ? g.pairs * g.nkb * H * 4 : 0), 256);
     g.off_downc = off;
     off = align_up(off + g.pairs * H * 4, 256);
     g.total = off;
     return g;
+}
+
+// Ring stage: the weight part (8 KB) and the B fragments of SK k-slices of up
+// to m rows; as many stages as fit the budget left after the two partial
+// tiles (2 x m x 128 floats), between 2 and 8.
+void ring_geom(int64_t m, bool precise, int* slot_bytes, int* ns) {
+    const int fw = precise ? 2 : 4;
+    *slot_bytes = kMoeWBytes + kMoeSK * (int) m * 16 * fw;
+    const int budget = kMoeRingBytes - 2 * (int) m * kCols * 4;
+    int n = budget / *slot_bytes;
+    *ns = n < 2 ? 2 : (n > 8 ? 8 : n);
+}
+
+// The largest case (32 rows, 4-word fragments): 2 stages of 24 KB + 32 KB of
+// partial tiles fit the budget.
+static_assert(2 * (kMoeWBytes + kMoeSK * kMoeMaxRows * 64) + 2 * kMoeMaxRows * kCols * 4 <= kMoeRingBytes,
+              "ring budget below 2 stages");
+int moe_smem_max() { return kMoeHeadBytes + kMoeRingBytes; }
+
+// Tensor-map templates per (hidden, intermediate): kind 0 = gate/up
+// [H/16][I/16][16K], kind 1 = down [I/16][H/16][16K]; box = [16K, 8, SK].
+// Encoded once on the host (cuTensorMapEncodeTiled through the runtime's
+// driver entry point) with a placeholder address that every unit replaces.
+struct MoeTemplates {
+    CUtensorMap t[8];
+};
+
+int encode_templates(int64_t H, int64_t I, void* placeholder, MoeTemplates* out) {
+    static std::mutex mu;
+    static std::map<std::pair<int64_t, int64_t>, MoeTemplates> cache;
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({H, I});
+    if (it != cache.end()) {
+        *out = it->second;
+        return EXL3_OK;
+    }
+    if (encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        EXL3_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        EXL3_REQUIRE(fn != nullptr && q == cudaDriverEntryPointSuccess, EXL3_ERR_CUDA,
+                     "moe: cuTensorMapEncodeTiled is not available from the driver");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    MoeTemplates T{};
+    for (int kind = 0; kind < 2; ++kind)
+        for (int K = 1; K <= kMoeKmax; ++K) {
+            const cuuint64_t ncols = (cuuint64_t) ((kind == 0 ? I : H) / 16);
+            const cuuint64_t nks = (cuuint64_t) ((kind == 0 ? H : I) / 16);
+            const cuuint64_t dims[3] = {(cuuint64_t) (16 * K), ncols, nks};
+            const cuuint64_t strides[2] = {(cuuint64_t) (32 * K), ncols * (cuuint64_t) (32 * K)};
+            const cuuint32_t box[3] = {(cuuint32_t) (16 * K), 8u, (cuuint32_t) kMoeSK};
+            const cuuint32_t estr[3] = {1u, 1u, 1u};
+            const CUresult r = encode(&T.t[kind * 4 + K - 1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, placeholder, dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            EXL3_REQUIRE(r == CUDA_SUCCESS, EXL3_ERR_CUDA, "moe: cuTensorMapEncodeTiled failed (%d) for K=%d",
+                         (int) r, K);
+        }
+    cache[{H, I}] = T;
+    *out = T;
+    return EXL3_OK;
 }
 
 struct MoePrepared {
@@ -563,11 +924,11 @@ int moe_prepare_cb(int dev, MoePrepared* out) {
     if (!pr.ready) {
         DeviceInfo di;
         if (int rc = device_info(dev, &di)) return rc;
-        const int smem = (int) sizeof(MoeSmem);
+        const int smem = moe_smem_max();
         auto kern = moe_kernel<CB, PRECISE>;
         EXL3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         int res = 0;
-        EXL3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, kern, kThreads, smem));
+        EXL3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, kern, kMoeThreads, smem));
         EXL3_REQUIRE(res > 0, EXL3_ERR_UNSUPPORTED, "moe kernel has no resident CTA");
         pr.sms = di.sms;
         pr.resident = res;
@@ -622,12 +983,29 @@ extern "C" int exl3_moe_info(int kmax, int64_t* info) {
     if (int rc = exl3_moe_prepare(kmax)) return rc;
     MoePrepared pr;
     if (int rc = moe_prepare_any(1, false, &pr)) return rc;
-    const int64_t v[14] = {pr.sms, pr.resident, kConsumerWarps + 1, pr.grid, kThreads, 3, MoeCfg::NS,
-                           kMoeMaxRows, (int64_t) sizeof(MoeSmem), EXL3_MOE_CTRL_BYTES,
+    int slot = 0, ns = 0;
+    ring_geom(4, false, &slot, &ns);
+    const int64_t v[14] = {pr.sms, pr.resident, kMoeThreads / 32, pr.grid, kMoeThreads, 3, ns,
+                           kMoeMaxRows, (int64_t) moe_smem_max(), EXL3_MOE_CTRL_BYTES,
                            exl3_moe_scratch_bytes(kMoeMaxRows, 8, 4096, 2048), kMoeMaxRows, kMoeMaxSlots, 1};
     for (int i = 0; i < 14; ++i) info[i] = v[i];
     return EXL3_OK;
 }
+
+#ifdef EXL3_PHASE_CLOCK
+// Phase-clock readout of the instrumented build (not part of the release
+// ABI): copies the accumulated per-phase cycle sums, optionally zeroing them.
+extern "C" int exl3_phase_clock_read(unsigned long long* out, int n, int reset) {
+    EXL3_REQUIRE(out && n >= 1 && n <= exl3::PH_N, EXL3_ERR_ARG, "phase clock: bad output");
+    EXL3_CUDA(cudaDeviceSynchronize());
+    EXL3_CUDA(cudaMemcpyFromSymbol(out, exl3::g_phase, sizeof(unsigned long long) * n));
+    if (reset) {
+        unsigned long long z[exl3::PH_N] = {};
+        EXL3_CUDA(cudaMemcpyToSymbol(exl3::g_phase, z, sizeof(z)));
+    }
+    return EXL3_OK;
+}
+#endif
 
 extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
                                int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
@@ -661,7 +1039,8 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     const MoeGeom g = moe_geom(m, topk, hidden, inter);
     EXL3_REQUIRE(scratch_bytes >= g.total, EXL3_ERR_ARG, "moe: scratch too small (%lld < %lld bytes)",
                  (long long) scratch_bytes, (long long) g.total);
-    EXL3_REQUIRE(g.kca % (MoeCfg::SK * 16) == 0 && g.kcb % (MoeCfg::SK * 16) == 0, EXL3_ERR_UNSUPPORTED,
+    EXL3_REQUIRE(g.kca % (kMoeSK * 16) == 0 && g.kcb % (kMoeSK * 16) == 0 && g.nka <= kMoeMaxNka &&
+                     g.nkb <= kMoeMaxNkb, EXL3_ERR_UNSUPPORTED,
                  "moe: internal k-chunks (%d, %d) do not tile the ring stages", g.kca, g.kcb);
     MoePrepared pr;
     if (int rc = moe_prepare_any(cb, precise != 0, &pr)) return rc;
@@ -687,30 +1066,34 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     p.kcb = g.kcb;
     p.nkb = g.nkb;
     uint8_t* sb = static_cast<uint8_t*>(scratch);
-    uint32_t* c32 = reinterpret_cast<uint32_t*>(sb);
-    p.ctrl = c32;
-    p.cntA = c32 + kCtrlWords;
-    p.readyB = p.cntA + kMoeMaxSlots * kStrideA;
-    p.cntB = p.readyB + kMoeMaxSlots * kStrideR;
-    p.cntG = p.cntB + kMoeMaxSlots * kStrideB;
+    EXL3_REQUIRE(pr.grid <= kMoeMaxGrid, EXL3_ERR_UNSUPPORTED, "moe: grid %d above %d", pr.grid, kMoeMaxGrid);
+    MoeTemplates tmpl;
+    if (int rc = encode_templates(hidden, inter, sb + g.off_tmaps, &tmpl)) return rc;
+    for (int i = 0; i < 8; ++i) p.tmpl[i] = tmpl.t[i];
+    p.tmaps = reinterpret_cast<CUtensorMap*>(sb + g.off_tmaps);
+    p.ctrl = reinterpret_cast<uint32_t*>(sb);
     p.partA = reinterpret_cast<float*>(sb + g.off_partA);
-    p.act = reinterpret_cast<__half*>(sb + g.off_act);
-    p.partB = reinterpret_cast<float*>(sb + g.off_partB);
+    p.xg = reinterpret_cast<uint32_t*>(sb + g.off_xg);
+    p.ag = reinterpret_cast<uint32_t*>(sb + g.off_ag);
     p.downc = reinterpret_cast<float*>(sb + g.off_downc);
+    // With a single k-chunk over I a block's partial is its full sum: the
+    // epilogue reads it and writes the transformed value in place.
+    p.partB = g.nkb > 1 ? reinterpret_cast<float*>(sb + g.off_partB) : p.downc;
+    ring_geom(m, precise != 0, &p.slot_bytes, &p.ns);
 
-    const int smem = (int) sizeof(MoeSmem);
+    const int smem = kMoeHeadBytes + p.ns * p.slot_bytes + 2 * (int) m * kCols * 4;
     auto s = static_cast<cudaStream_t>(stream);
     if (precise) {
         switch (cb) {
-            case 0: moe_kernel<0, true><<<pr.grid, kThreads, smem, s>>>(p); break;
-            case 1: moe_kernel<1, true><<<pr.grid, kThreads, smem, s>>>(p); break;
-            default: moe_kernel<2, true><<<pr.grid, kThreads, smem, s>>>(p); break;
+            case 0: moe_kernel<0, true><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
+            case 1: moe_kernel<1, true><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
+            default: moe_kernel<2, true><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
         }
     } else {
         switch (cb) {
-            case 0: moe_kernel<0, false><<<pr.grid, kThreads, smem, s>>>(p); break;
-            case 1: moe_kernel<1, false><<<pr.grid, kThreads, smem, s>>>(p); break;
-            default: moe_kernel<2, false><<<pr.grid, kThreads, smem, s>>>(p); break;
+            case 0: moe_kernel<0, false><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
+            case 1: moe_kernel<1, false><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
+            default: moe_kernel<2, false><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
         }
     }
     EXL3_CUDA(cudaGetLastError());
@@ -724,7 +1107,7 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
 // graph), hosts whose memory is owned by another allocator and who therefore
 // cannot hand out a scratch buffer, and latency-critical callers that cannot
 // afford cudaMalloc's implicit synchronization.  Its scratch is the array
-// below, compiled into the library: EXL3_MOE_STATIC_SCRATCH_BYTES (4 MiB) of
+// below, compiled into the library: EXL3_MOE_STATIC_SCRATCH_BYTES (8 MiB) of
 // device memory that every GPU which loads the library holds until the
 // process exits.  Geometries whose scratch (exl3_moe_scratch_bytes) exceeds it
 // are rejected.

@@ -136,18 +136,18 @@ int exl3_moe_info(int kmax, int64_t* info);
  * reference.  For callers that may not allocate device memory: code running
  * inside CUDA graph capture, hosts whose device memory belongs to another
  * allocator, callers that cannot take cudaMalloc's synchronization.  Same
- * arguments as exl3_moe_decode minus the scratch: the scratch is a
- * 4 MiB array compiled into the library (EXL3_MOE_STATIC_SCRATCH_BYTES),
+ * arguments as exl3_moe_decode minus the scratch: the scratch is an
+ * 8 MiB array compiled into the library (EXL3_MOE_STATIC_SCRATCH_BYTES),
  * held on every GPU that loads the library until the process exits.
  * Geometries whose exl3_moe_scratch_bytes() exceeds it are rejected with
- * EXL3_ERR_ARG (4 MiB covers m <= 16 rows at top-8, hidden 4096,
+ * EXL3_ERR_ARG (8 MiB covers m <= 16 rows at top-8, hidden 4096,
  * intermediate 256, and m <= 4 at intermediate 2048).  Each call clears the
  * array's control region with cudaMemsetAsync on `stream`, then launches.
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) and should come before any stream capture.  All
  * calls on a device share the one array: calls that can overlap on the GPU
  * (different streams without ordering) race and must not be issued. */
-#define EXL3_MOE_STATIC_SCRATCH_BYTES (4 << 20)
+#define EXL3_MOE_STATIC_SCRATCH_BYTES (8 << 20)
 int exl3_moe_decode_noalloc(const void* x, int x_dtype, void* out, int out_dtype,
                             int64_t m, int64_t hidden, int64_t inter,
                             const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,

@@ -1,7 +1,7 @@
 """exl3_moe_decode_noalloc: the routed-MoE layer for callers that may not
 allocate device memory (code inside CUDA graph capture, hosts whose device
 memory belongs to another allocator, callers that cannot take cudaMalloc's
-synchronization).  Its scratch is a 4 MiB array compiled into the library.
+synchronization).  Its scratch is an 8 MiB array compiled into the library.
 
 Called through the C ABI twice in a row (the array keeps the first call's
 contents, which the second call must not depend on); each result is compared
