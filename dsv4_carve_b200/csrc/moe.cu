@@ -51,7 +51,8 @@ constexpr int kMoeKmax = 4;          // weight part of a ring stage sized for K 
 constexpr int kMoeMaxHidden = 8192;
 constexpr int kMoeMaxInter = 4096;
 constexpr int kMoeSK = 8;                                 // k-slices per ring stage
-constexpr int kMoeWBytes = kMoeSK * 8 * 32 * kMoeKmax;    // weight part of a stage (8 KB)
+constexpr int kMoeWBytes = kMoeSK * 8 * 32 * kMoeKmax;    // largest weight part of a stage (8 KB)
+constexpr int kMoeMaxStages = 12;                         // ring depth cap
 constexpr int kMoeRingBytes = 98304;                      // ring + partial tiles per CTA
 constexpr int kMoeDQ = 4;                                 // descriptor queue depth
 constexpr int kMoeMaxNka = 8;                             // hidden k-chunks
@@ -128,9 +129,9 @@ static __device__ unsigned long long g_phase[PH_N];
 // template to shared memory, replaces the address with its expert's matrix
 // and publishes it to a per-CTA global slot.  A slot is rewritten only after
 // every copy issued through it has landed: slots are used round robin and
-// kMoeTmapSlots exceeds the ring depth (<= 8 stages, >= 1 stage per unit).
-constexpr int kMoeTmapSlots = 9;
-constexpr int kMoeMaxGrid = 512;
+// kMoeTmapSlots exceeds the ring depth (<= 12 stages, >= 1 stage per unit).
+constexpr int kMoeTmapSlots = 13;
+constexpr int kMoeMaxGrid = 320;   // 2 CTAs per SM on up to 160 SMs
 
 struct MoeParams {
     CUtensorMap tmpl[8];        // [kind (0 gate/up, 1 down)][K - 1]
@@ -147,6 +148,7 @@ struct MoeParams {
     int kca, nka;               // gate/up k-chunk over H
     int kcb, nkb;               // down k-chunk over I
     int slot_bytes, ns;         // ring: ns stages of slot_bytes (weights, then B fragments)
+    int wpart;                  // weight part of a stage: SK x 8 tiles x 32 * kmax bytes
     uint32_t* ctrl;
     float* partA;               // [pairs][2][nka][I]
     uint32_t* xg;               // input fragments: per pair 2 * (H/16) row-slices of 16*FW bytes
@@ -239,8 +241,8 @@ __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
 
 struct alignas(128) MoeHead {
     MoePlan plan;
-    uint64_t full[8];
-    uint64_t empty[8];
+    uint64_t full[kMoeMaxStages];
+    uint64_t empty[kMoeMaxStages];
     uint64_t dqf[kMoeDQ];
     uint64_t dqe[kMoeDQ];
     uint64_t pfull[2];          // partial tile written by the consumer warps
@@ -300,7 +302,7 @@ __device__ __forceinline__ bool moe_consume(const MoeParams& p, uint8_t* ring, u
             phi[h] = base + cwarp * F::WORDS + geom.ihi[h];
             plo[h] = base + cwarp * F::WORDS + geom.ilo[h];
         }
-        const uint32_t* bf = base + kMoeWBytes / 4;
+        const uint32_t* bf = base + p.wpart / 4;
 #pragma unroll
         for (int i = 0; i < kMoeSK; ++i) {
             uint32_t whi[F::NG], wlo[F::NG];
@@ -544,7 +546,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                     s = r % p.nkb;
                 }
                 int K = p.ktab ? p.ktab[P.gexp[g]] : p.kuni;
-                if (K < 1 || K > kMoeKmax) K = 0;
+                if (K < 1 || 256 * K * kMoeSK > p.wpart) K = 0;   // above the launch's kmax: stage too small
                 d[0] = kind; d[1] = g; d[2] = mat; d[3] = blk; d[4] = s; d[5] = K;
             }
             if (lane == 0) {
@@ -565,6 +567,10 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 ticket = claim_ticket(&p.ctrl[0], lane);
                 continue;
             }
+            // claim the next unit now; its atomic completes while this unit's
+            // stages are issued
+            int next_raw = 0;
+            if (lane == 0) next_raw = (int) atomicAdd(&p.ctrl[0], 1u);
             const int kind = d[0], g = d[1], mat = d[2], blk = d[3], s = d[4], K = d[5];
             const int e = P.gexp[g];
             const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
@@ -617,7 +623,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                         if (valid) {
                             mbar_arrive_expect_tx(&S.full[slot], wbytes + (uint32_t) bbytes);
                             tma_load_3d(dst, gtm, 0, blk * 8, ks0 + st * kMoeSK, &S.full[slot]);
-                            bulk_g2s(dst + kMoeWBytes, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
+                            bulk_g2s(dst + p.wpart, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
                         } else {
                             mbar_arrive(&S.full[slot]);
                         }
@@ -628,7 +634,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 ++it;
                 PHASE_MARK(PH_PROD_ISSUE);
             }
-            ticket = claim_ticket(&p.ctrl[0], lane);
+            ticket = __shfl_sync(0xffffffffu, next_raw, 0);
         }
         // no bulk copy may still be writing shared memory when the CTA retires
         if (lane == 0) {
@@ -846,15 +852,16 @@ MoeGeom moe_geom(int64_t m, int64_t topk, int64_t H, int64_t I) {
     return g;
 }
 
-// Ring stage: the weight part (8 KB) and the B fragments of SK k-slices of up
-// to m rows; as many stages as fit the budget left after the two partial
-// tiles (2 x m x 128 floats), between 2 and 8.
-void ring_geom(int64_t m, bool precise, int* slot_bytes, int* ns) {
+// Ring stage: the weight part (SK k-slices x 8 tiles at the launch's largest
+// K) and the B fragments of SK k-slices of up to m rows; as many stages as fit
+// the budget left after the two partial tiles (2 x m x 128 floats), 2 to 12.
+void ring_geom(int64_t m, int kmax, bool precise, int* wpart, int* slot_bytes, int* ns) {
     const int fw = precise ? 2 : 4;
-    *slot_bytes = kMoeWBytes + kMoeSK * (int) m * 16 * fw;
+    *wpart = kMoeSK * 8 * 32 * kmax;
+    *slot_bytes = *wpart + kMoeSK * (int) m * 16 * fw;
     const int budget = kMoeRingBytes - 2 * (int) m * kCols * 4;
     int n = budget / *slot_bytes;
-    *ns = n < 2 ? 2 : (n > 8 ? 8 : n);
+    *ns = n < 2 ? 2 : (n > kMoeMaxStages ? kMoeMaxStages : n);
 }
 
 // The largest case (32 rows, 4-word fragments): 2 stages of 24 KB + 32 KB of
@@ -984,7 +991,8 @@ extern "C" int exl3_moe_info(int kmax, int64_t* info) {
     MoePrepared pr;
     if (int rc = moe_prepare_any(1, false, &pr)) return rc;
     int slot = 0, ns = 0;
-    ring_geom(4, false, &slot, &ns);
+    int wpart = 0;
+    ring_geom(4, kmax, false, &wpart, &slot, &ns);
     const int64_t v[14] = {pr.sms, pr.resident, kMoeThreads / 32, pr.grid, kMoeThreads, 3, ns,
                            kMoeMaxRows, (int64_t) moe_smem_max(), EXL3_MOE_CTRL_BYTES,
                            exl3_moe_scratch_bytes(kMoeMaxRows, 8, 4096, 2048), kMoeMaxRows, kMoeMaxSlots, 1};
@@ -1079,7 +1087,7 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     // With a single k-chunk over I a block's partial is its full sum: the
     // epilogue reads it and writes the transformed value in place.
     p.partB = g.nkb > 1 ? reinterpret_cast<float*>(sb + g.off_partB) : p.downc;
-    ring_geom(m, precise != 0, &p.slot_bytes, &p.ns);
+    ring_geom(m, k_table ? kmax : K, precise != 0, &p.wpart, &p.slot_bytes, &p.ns);
 
     const int smem = kMoeHeadBytes + p.ns * p.slot_bytes + 2 * (int) m * kCols * 4;
     auto s = static_cast<cudaStream_t>(stream);
