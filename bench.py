@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--tokens", type=int, default=4)
     ap.add_argument("--route", choices=["uniform", "zipf"], default="uniform")
+    ap.add_argument("--config", choices=["moe", "dense"], default="moe",
+                    help="moe: config 2/3 routed-MoE layer (the headline); dense: config 1 K6 linears")
+    ap.add_argument("--rows", type=int, default=4, help="dense: activation rows R")
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--precise", action="store_true", help="fp16-rounded weights in the MMA")
     ap.add_argument("--no-e2e", action="store_true")
@@ -226,6 +229,123 @@ class MoeWorkload:
     def bytes_per_step(self, i):
         return self.ubytes[i % len(self.layers)]
 
+    launches_per_step = 1
+    kernel_name = "exl3::moe_kernel"
+    metric = None
+
+    def describe(self):
+        a = self.args
+        return {"workload": "config2_moe_decode_layer" if a.route == "uniform" else "config3_moe_decode_layer_zipf",
+                "tokens": a.tokens, "topk": 8, "experts": a.experts, "hidden": 4096, "intermediate": 2048,
+                "intermediate_per_gpu": 2048 // self.world, "route": a.route, "layers_cycled": a.layers,
+                "unique_experts_per_layer": self.uniq,
+                "parallelism": f"tp{self.world}" if self.world > 1 else "single",
+                "l2": "inputs larger than L2 (unique bytes per layer > 126 MB; layers cycled)",
+                "precise": bool(a.precise)}
+
+
+class DenseWorkload:
+    """Config 1: the dense EXL3 6-bit linears of attention / shared experts,
+    [4096 -> 4096], [4096 -> 1536], [1536 -> 4096], K = 6, 3INST, R rows of
+    fp16 N(0,1).  A step applies the three linears to one batch; sets of the
+    three matrices are cycled so that steps stream from HBM (8 sets = 176 MB).
+    TP: the two 4096-input matrices are column-sharded in whole 128-column
+    blocks, [1536 -> 4096] is row-sharded and its partial output all-reduced."""
+
+    launches_per_step = 3
+    kernel_name = "exl3::linear_kernel"
+    metric = "dense EXL3 K6 linear set (config 1: [4096->4096], [4096->1536], [1536->4096]): packed-weight HBM GB/s"
+
+    def __init__(self, args, rank, world, dev):
+        import torch
+
+        from dsv4_carve_b200 import _lib, synth
+        from dsv4_carve_b200 import vllm_exl3_c as ext
+
+        self.torch, self.ext, self.args, self.world, self.dev = torch, ext, args, world, dev
+        self.R = args.rows
+        self.lib = _lib.load()
+        self.sets, self.xs, self.ys, self.argv, self.nbytes = [], [], [], [], []
+        shapes = [(4096, 4096, "col"), (4096, 1536, "col"), (1536, 4096, "row")]
+        nsets = max(1, args.layers * 2)
+        for si in range(nsets):
+            mats = []
+            for mi, (k, n, mode) in enumerate(shapes):
+                w = synth.make_dense(k, n, 6, seed=5000 + 10 * si + mi, device=dev, cb=synth.CB_3INST)
+                if world > 1:
+                    w = synth.shard_col_blocks(w, rank, world) if mode == "col" else synth.shard_row_blocks(w, rank, world)
+                mats.append(w)
+            self.sets.append(mats)
+        scratch_need = max(self.lib.exl3_linear_scratch_bytes(self.R, m.in_features, m.out_features, 6)
+                           for mats in self.sets for m in mats)
+        self.scratch = torch.zeros(scratch_need, dtype=torch.uint8, device=dev)
+        x = synth.activations(self.R, 4096, seed=77, device=dev)
+        for mats in self.sets:
+            a, b, c = mats
+            xin_c = synth.activations(self.R, c.in_features, seed=78, device=dev)
+            outs = [torch.empty((self.R, m.out_features), dtype=torch.float16, device=dev) for m in mats]
+            ins = [x, x, xin_c]
+            argv = []
+            for m, xi, yo in zip(mats, ins, outs):
+                argv.append((xi.data_ptr(), _lib.DT_F16, self.R, m.in_features, m.out_features, m.trellis.data_ptr(),
+                             6, synth.CB_3INST, m.suh.data_ptr(), m.svh.data_ptr(), yo.data_ptr(), _lib.DT_F16,
+                             self.scratch.data_ptr(), self.scratch.numel(), 1))
+            self.argv.append(argv)
+            self.xs.append(ins)
+            self.ys.append(outs)
+            self.nbytes.append(sum(m.nbytes() + self.R * 2 * (m.in_features + m.out_features) for m in mats))
+        self.h_x = [t.cpu().pin_memory() for t in (x,)]
+        self.h_y = torch.empty((self.R, 4096), dtype=torch.float16).pin_memory()
+        self.h2d = self.R * 4096 * 2
+        self.d2h = self.R * 4096 * 2
+        self.uniq = []
+
+    def launch(self, i, stream_handle):
+        for a in self.argv[i % len(self.argv)]:
+            rc = self.lib.exl3_linear(*a, stream_handle)
+            if rc:
+                raise RuntimeError(self.lib.exl3_last_error().decode())
+
+    def allreduce(self, out):
+        if self.world > 1:
+            self.torch.distributed.all_reduce(out)
+
+    @property
+    def outs(self):
+        return [ys[2] for ys in self.ys]
+
+    @property
+    def layers(self):
+        return self.sets
+
+    def step(self, i, stream_handle):
+        self.launch(i, stream_handle)
+        self.allreduce(self.outs[i % len(self.sets)])
+
+    def e2e_step(self, i):
+        """x from pinned host memory, the three linears through the public
+        linear_forward call, the last output back to pinned host memory."""
+        torch = self.torch
+        si = i % len(self.sets)
+        x = self.xs[si][0]
+        x.copy_(self.h_x[0], non_blocking=True)
+        a, b, c = self.sets[si]
+        ya = self.ext.linear_forward(x, a.trellis, a.suh, a.svh, 6, 0, torch.float16, True)
+        yb = self.ext.linear_forward(x, b.trellis, b.suh, b.svh, 6, 0, torch.float16, True)
+        yc = self.ext.linear_forward(self.xs[si][2], c.trellis, c.suh, c.svh, 6, 0, torch.float16, True)
+        self.allreduce(yc)
+        self.h_y.copy_(yc, non_blocking=True)
+        return ya, yb
+
+    def bytes_per_step(self, i):
+        return self.nbytes[i % len(self.sets)]
+
+    def describe(self):
+        return {"workload": "config1_dense_k6_linear_set", "rows": self.R, "K": 6, "codebook": "3INST",
+                "matrices": ["4096x4096", "4096x1536", "1536x4096"], "sets_cycled": len(self.sets),
+                "parallelism": f"tp{self.world}" if self.world > 1 else "single",
+                "l2": "sets cycled: 8 x 22 MB > 126 MB L2", "precise": True}
+
 
 # ----------------------------------------------------------------------------- CPU baseline
 _CPU_CACHE: dict = {}
@@ -341,7 +461,7 @@ def main():
         if world > 1:
             torch.distributed.barrier(device_ids=[local])
 
-    wl = MoeWorkload(args, rank, world, dev)
+    wl = (DenseWorkload if args.config == "dense" else MoeWorkload)(args, rank, world, dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     for i in range(args.warmup):
@@ -426,33 +546,30 @@ def main():
     bytes_per_launch = my_bytes / K
     achieved = bytes_per_launch / (kern_avg_ms / 1e3) / 1e9
     traffic = None
-    if NCU_TRAFFIC_FILE.exists() and world == 1:
+    if NCU_TRAFFIC_FILE.exists() and world == 1 and args.config == "moe":
         try:
             tr = json.loads(NCU_TRAFFIC_FILE.read_text())
-            traffic = tr.get("dram_bytes_per_launch")
+            # captured launch's DRAM bytes, scaled to this run's algorithmic bytes per launch
+            traffic = tr["dram_bytes_per_launch"] / tr["algorithmic_bytes_per_launch"] * (my_bytes / K)
         except Exception:
             traffic = None
+    rows = args.rows if args.config == "dense" else args.tokens
     line = {
-        "metric": METRIC, "value": all_bytes / (ms_max / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
+        "metric": wl.metric or METRIC, "value": all_bytes / (ms_max / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
         "steps": K, "warmup": args.warmup, "ms_per_step": ms_max / K, "us_per_layer": ms_max / K * 1e3,
-        "tokens_per_s_per_layer": args.tokens * K / (ms_max / 1e3),
+        "tokens_per_s_per_layer": rows * K / (ms_max / 1e3),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-        "dtype": "u16 trellis (K2/K3) -> fp16 MMA, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": "config2_moe_decode_layer", "tokens": args.tokens, "topk": 8, "experts": args.experts,
-                   "hidden": 4096, "intermediate": 2048, "intermediate_per_gpu": 2048 // world,
-                   "route": args.route, "layers_cycled": args.layers,
-                   "unique_experts_per_layer": wl.uniq, "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (unique bytes per layer > 126 MB; layers cycled)",
-                   "precise": bool(args.precise)},
-        "roofline": {"bound": "hbm", "kernel": "exl3::moe_kernel", "achieved": achieved, "peak": peak,
+        "dtype": "u16 trellis -> fp16 MMA, fp32 accumulate", "data": "synthetic",
+        "config": wl.describe(),
+        "roofline": {"bound": "hbm", "kernel": wl.kernel_name, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
                      "kernel_us_avg": kern_avg_ms * 1e3},
-        "gpu_launches": K,
+        "gpu_launches": K * wl.launches_per_step,
         "e2e": e2e,
         "clocks": clock_info,
     }
-    if world == 1 and not args.no_cpu:
+    if world == 1 and not args.no_cpu and args.config == "moe":
         v, desc, cores, kind, dt, _ = cpu_reference_sample(args, args.cpu_seconds)
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc,
                                 "seconds": dt}

@@ -137,7 +137,7 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 }
 
 // 3-D tiled TMA load of one box into this CTA's shared memory, completion
-// counted in bytes on an mbarrier.  No multicast.  The innermost coordinate
+// counted in bytes on an mbarrier; this CTA only.  The innermost coordinate
 // is always 0 here (whole 16-bit tiles), so it is 16-byte aligned.
 __device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
     asm volatile(
@@ -164,7 +164,7 @@ __device__ __forceinline__ void tmap_acquire(const void* gmem_tmap) {
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completion counted in bytes
-// on an mbarrier.  No multicast (plain per-CTA copy).
+// on an mbarrier (plain per-CTA copy).
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
                                          uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

@@ -95,6 +95,35 @@ def shard_row(w: DenseWeight, rank: int, world: int) -> DenseWeight:
                        w.suh[rank * c * 16:(rank + 1) * c * 16].contiguous(), w.svh, w.K, w.cb)
 
 
+def block_range(nblocks: int, rank: int, world: int) -> tuple:
+    """Whole 128-wide Hadamard blocks of a dimension split over `world` ranks
+    as evenly as possible (e.g. 1536 = 12 blocks over 8 ranks: 2,2,2,2,1,1,1,1).
+    Returns (first block, block count) of `rank`."""
+    base, extra = divmod(nblocks, world)
+    return rank * base + min(rank, extra), base + (1 if rank < extra else 0)
+
+
+def shard_col_blocks(w: DenseWeight, rank: int, world: int) -> DenseWeight:
+    """Column parallel in whole 128-column blocks (uneven when the block count
+    does not divide by the world size)."""
+    if world == 1:
+        return w
+    b0, nb = block_range(w.out_features // 128, rank, world)
+    assert nb > 0, "more ranks than 128-column blocks"
+    t = w.trellis[:, b0 * 8:(b0 + nb) * 8].contiguous()
+    return DenseWeight(t, w.suh, w.svh[b0 * 128:(b0 + nb) * 128].contiguous(), w.K, w.cb)
+
+
+def shard_row_blocks(w: DenseWeight, rank: int, world: int) -> DenseWeight:
+    """Row parallel in whole 128-row blocks (the partial outputs are summed)."""
+    if world == 1:
+        return w
+    b0, nb = block_range(w.in_features // 128, rank, world)
+    assert nb > 0, "more ranks than 128-row blocks"
+    t = w.trellis[b0 * 8:(b0 + nb) * 8].contiguous()
+    return DenseWeight(t, w.suh[b0 * 128:(b0 + nb) * 128].contiguous(), w.svh, w.K, w.cb)
+
+
 @dataclass
 class MoeLayer:
     """One routed-MoE layer (possibly a TP shard) with the plugin's 9 pointer tables."""
