@@ -7,10 +7,13 @@
 // as the reference: input fp16(x) * suh in fp16, 128-block Hadamard in fp32
 // rounded to fp16, fp32 accumulation, output Hadamard and svh in fp32, one
 // cast to the output dtype.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
-#include "engine.cuh"
 #include "host.hpp"
+#include "stage.cuh"
 
 namespace exl3 {
 
@@ -98,197 +101,278 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const uint8_t* __restr
 }
 
 // ------------------------------------------------------------------ linear
+// One persistent launch per (<= 32-row) block of rows, the same CTA roles as
+// the routed-MoE kernel: warps 0-7 decode + MMA, warp 8 produces (unit
+// tickets, one 3-D TMA box of weights plus one bulk copy of B fragments per
+// ring stage), warp 9 stores each unit's partial tile, counts completions per
+// 128-column block and finishes the block.  Units are (128-column block, k-chunk)
+// in block-major order.  Before their first unit the consumer warps transform
+// the input once per launch (x -> fp16, * suh in fp16, 128-point Hadamard in
+// fp32 -> fp16) straight into B-fragment order; the producer waits (bounded)
+// for a chunk's fragments before copying them.  The finisher sums a block's
+// chunk partials in fixed order and applies Hadamard * svh and the cast, so
+// results are bitwise reproducible.
+constexpr int kLinConsumerWarps = 8;
+constexpr int kLinProducerWarp = 8;
+constexpr int kLinEpilogueWarp = 9;
+constexpr int kLinThreads = 320;
+constexpr int kLinMaxRows = 32;
+constexpr int kLinMaxChunks = 8;             // k-chunks per 128-column block
+constexpr int kLinRingBytes = 98304;         // ring + partial tiles
+constexpr int kLinMaxStages = 12;
+constexpr int kLinDQ = 4;
+// control words: [0] unit ticket [1] retired CTAs [2] status [3] input items,
+// readyP[kLinMaxChunks] at 16, block counters at 16 + kLinMaxChunks
+constexpr int kLinOffReady = 16;
+constexpr int kLinOffCnt = kLinOffReady + kLinMaxChunks;
+
 struct LinearParams {
+    CUtensorMap tmap;           // trellis as [k/16][n/16][16K] u16, box [16K, 8, SK]
     const void* x;
     int x_dtype;
-    int rows;            // <= kMaxRows
-    int64_t k, n;
-    const uint8_t* trellis;
+    int rows;
+    int k, n;
     const __half* suh;
     const __half* svh;
     void* y;
     int y_dtype;
-    int kc;              // k-chunk per unit (multiple of 128 and of the stage depth)
-    int nchunks;         // k / kc
-    float* partial;      // [nchunks][rows][n]
-    uint32_t* colcnt;    // [n/128]
-    uint32_t* ctrl;      // [0] ticket, [1] retire, [2] status
+    int kc, nk;                 // k-chunk per unit, chunk count
+    RingGeom ring;
+    uint32_t* ctrl;
+    uint32_t* xg;               // B fragments [k/16][rows][4][FW]
+    float* partial;             // [nk][rows][n]
 };
 
-template <int K> struct LinCfg {
-    static constexpr int SK = stage_slices(K);
-    static constexpr int STAGE = SK * 8 * TileFmt<K>::BYTES;
-    static constexpr int NS = (49152 / STAGE) > 8 ? 8 : (49152 / STAGE);
+struct alignas(128) LinHead {
+    uint64_t full[kLinMaxStages];
+    uint64_t empty[kLinMaxStages];
+    uint64_t dqf[kLinDQ];
+    uint64_t dqe[kLinDQ];
+    uint64_t pfull[2];
+    uint64_t pempty[2];
+    int desc[kLinDQ][4];        // valid, block, chunk
+    int last_cta;
 };
-
-template <int K>
-struct alignas(128) LinSmem {
-    uint8_t ring[LinCfg<K>::NS][LinCfg<K>::STAGE];
-    uint4 bfrag[kActBytes / 16];
-    float cbuf[kMaxRows * kCols];
-    uint64_t full[LinCfg<K>::NS];
-    uint64_t empty[LinCfg<K>::NS];
-    uint64_t dqf[kDQ];
-    uint64_t dqe[kDQ];
-    int desc[kDQ][2];
-    int rows[kMaxRows];
-    int flag;
-};
-
-template <int K, int CB, int RB, bool PRECISE>
-__device__ __forceinline__ bool lin_consume(LinSmem<K>& S, uint32_t& it, int nst, float (&acc)[4][4],
-                                            const LaneGeom<K>& geom, int cwarp, int lane, uint32_t* status) {
-    return consume_stages<K, CB, RB, LinCfg<K>::NS, LinCfg<K>::STAGE, LinCfg<K>::SK, PRECISE>(
-        S.ring, S.full, S.empty, it, nst, 0, S.bfrag, acc, geom, cwarp, lane, status);
-}
+constexpr int kLinHeadBytes = (int) ((sizeof(LinHead) + 127) / 128 * 128);
 
 template <int K, int CB, bool PRECISE>
-__global__ void __launch_bounds__(kThreads, 2) linear_kernel(LinearParams p) {
-    using C = LinCfg<K>;
+__global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_constant__ LinearParams p) {
+    constexpr int FW = Frag<PRECISE>::FW;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    LinSmem<K>& S = *reinterpret_cast<LinSmem<K>*>(smem_raw);
+    LinHead& S = *reinterpret_cast<LinHead*>(smem_raw);
+    uint8_t* ring = smem_raw + kLinHeadBytes;
+    float* ptile = reinterpret_cast<float*>(ring + (size_t) p.ring.ns * p.ring.slot_bytes);   // [2][rows][128]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t* status = p.ctrl + 2;
+    uint32_t* readyP = p.ctrl + kLinOffReady;
+    uint32_t* cnt = p.ctrl + kLinOffCnt;
+    const int NB = p.n / kCols;
+    const int total = NB * p.nk;
+    const int rows = p.rows;
 
     if (tid == 0) {
-        for (int s = 0; s < C::NS; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kConsumerWarps); }
-        for (int s = 0; s < kDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], 1); }
+        for (int s = 0; s < p.ring.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kLinConsumerWarps); }
+        for (int s = 0; s < kLinDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], kLinConsumerWarps + 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&S.pfull[s], kLinConsumerWarps); mbar_init(&S.pempty[s], 1); }
         fence_barrier_init();
     }
-    if (tid < kMaxRows) S.rows[tid] = tid;
     __syncthreads();
 
-    const int nbn = (int) (p.n / kCols);
-    const int total = nbn * p.nchunks;
-    const int kslices = p.kc / 16;
-    const int nst = kslices / C::SK;
-
-    if (warp == kProducerWarp) {
-        // ---------------------------------------------------------- producer
-        const int rowbytes = 8 * TileFmt<K>::BYTES;
-        const int64_t rowstride = (p.n / 16) * TileFmt<K>::BYTES;
+    if (warp == kLinProducerWarp) {
+        // ------------------------------------------------------------ producer
         int ticket = claim_ticket(&p.ctrl[0], lane);
         uint32_t it = 0, du = 0;
         bool ok = true;
+        const int64_t rsb = (int64_t) rows * 16 * FW;          // fragment bytes per k-slice
+        const int bbytes = (int) (kStageSK * rsb);
+        const uint32_t wbytes = (uint32_t) (kStageSK * 8 * 32 * K);
+        const int nst = p.kc / (16 * kStageSK);
         while (ok) {
             const bool end = ticket >= total;
-            const int j = end ? -1 : ticket / p.nchunks;
-            const int s = end ? -1 : ticket % p.nchunks;
+            const int blk = end ? 0 : ticket / p.nk, s = end ? 0 : ticket % p.nk;
+            int next_raw = 0;
+            if (!end && lane == 0) next_raw = (int) atomicAdd(&p.ctrl[0], 1u);
             if (lane == 0) {
-                const int slot = du % kDQ;
-                ok = mbar_wait(&S.dqe[slot], ((du / kDQ) + 1u) & 1u, status);
+                const int slot = du % kLinDQ;
+                ok = mbar_wait(&S.dqe[slot], ((du / kLinDQ) + 1u) & 1u, status);
                 if (ok) {
-                    S.desc[slot][0] = j;
-                    S.desc[slot][1] = s;
+                    S.desc[slot][0] = end ? 0 : 1;
+                    S.desc[slot][1] = blk;
+                    S.desc[slot][2] = s;
                     mbar_arrive(&S.dqf[slot]);
                 }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             ++du;
             if (end || !ok) break;
-            const uint8_t* src = p.trellis + (int64_t) s * kslices * rowstride + (int64_t) j * rowbytes;
-            const bool valid = aligned16_dev(src) && (rowstride & 15) == 0;
-            if (!valid && lane == 0) set_error(status, ERR_MISALIGNED);
-            for (int st = 0; st < nst && ok; ++st)
-                ok = produce_stage<C::NS, C::STAGE>(S.ring, S.full, S.empty, it, src + (int64_t) st * C::SK * rowstride,
-                                                    rowstride, rowbytes, C::SK, valid, lane, status);
-            ticket = claim_ticket(&p.ctrl[0], lane);
+            if (lane == 0) {
+                wait_counter(&readyP[s], (uint32_t) (p.kc / kCols * rows), status);
+                fence_proxy_async_global();
+            }
+            __syncwarp();
+            const int ks0 = s * (p.kc / 16);
+            const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.xg) + (int64_t) ks0 * rsb;
+            for (int st = 0; st < nst && ok; ++st) {
+                const int slot = (int) (it % (uint32_t) p.ring.ns);
+                if (lane == 0) {
+                    ok = mbar_wait(&S.empty[slot], ((it / (uint32_t) p.ring.ns) + 1u) & 1u, status);
+                    if (ok) {
+                        uint8_t* dst = ring + (size_t) slot * p.ring.slot_bytes;
+                        mbar_arrive_expect_tx(&S.full[slot], wbytes + (uint32_t) bbytes);
+                        tma_load_3d(dst, &p.tmap, 0, blk * 8, ks0 + st * kStageSK, &S.full[slot]);
+                        bulk_g2s(dst + p.ring.wpart, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                ++it;
+            }
+            ticket = __shfl_sync(0xffffffffu, next_raw, 0);
         }
-        drain_ring<C::NS>(S.full, it, lane, status);
-    } else {
-        // ---------------------------------------------------------- consumers
-        const int ctid = tid;
-        const LaneGeom<K> geom = lane_geom<K>(lane);
-        const int RB = row_blocks(p.rows);
-        const int sub = (act_slices(RB) / 16) * 16 < kslices ? (act_slices(RB) / 16) * 16 : kslices;
-        uint32_t it = 0, du = 0;
+        // no bulk copy may still be writing shared memory when the CTA retires
+        if (lane == 0) {
+            const uint32_t first = it > (uint32_t) p.ring.ns ? it - (uint32_t) p.ring.ns : 0u;
+            for (uint32_t i = first; i < it; ++i)
+                if (!mbar_wait(&S.full[i % p.ring.ns], (i / p.ring.ns) & 1u, status)) break;
+        }
+    } else if (warp == kLinEpilogueWarp) {
+        // ------------------------------------------------------------ epilogue
+        uint32_t du = 0, uu = 0;
         while (true) {
-            const int slot = du % kDQ;
-            if (!consumers_all(mbar_wait_warp(&S.dqf[slot], (du / kDQ) & 1u, status, lane))) break;
-            const int j = S.desc[slot][0], s = S.desc[slot][1];
-            consumers_sync();
-            if (ctid == 0) mbar_arrive(&S.dqe[slot]);
+            const int slot = du % kLinDQ;
+            if (!mbar_wait_lanes(&S.dqf[slot], (du / kLinDQ) & 1u, status)) break;
+            const int valid = S.desc[slot][0], blk = S.desc[slot][1], s = S.desc[slot][2];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
-            if (j < 0) break;
-
+            if (!valid) break;
+            const int ps = (int) (uu & 1u);
+            if (!mbar_wait_lanes(&S.pfull[ps], (uu >> 1) & 1u, status)) break;
+            const float* tile = ptile + (size_t) ps * rows * kCols;
+            for (int r = 0; r < rows; ++r) {
+                const float4 v = *reinterpret_cast<const float4*>(tile + r * kCols + lane * 4);
+                __stcg(reinterpret_cast<float4*>(p.partial + ((int64_t) s * rows + r) * p.n + blk * kCols + lane * 4), v);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.pempty[ps]);
+            ++uu;
+            int last = 0;
+            if (lane == 0) {
+                const uint32_t old = atom_add_release_gpu(&cnt[blk], 1u);
+                last = old == (uint32_t) (p.nk - 1);
+                if (last) {
+                    atomicExch(&cnt[blk], 0u);
+                    fence_acq_rel_gpu();
+                }
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            for (int r = 0; r < rows; ++r) {
+                // all chunk partials of the row in flight at once, summed in chunk order
+                float4 a[kLinMaxChunks];
+#pragma unroll
+                for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
+                    if (c2 < p.nk)
+                        a[c2] = __ldcg(reinterpret_cast<const float4*>(
+                            p.partial + ((int64_t) c2 * rows + r) * p.n + blk * kCols + lane * 4));
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
+                    if (c2 < p.nk) { v[0] += a[c2].x; v[1] += a[c2].y; v[2] += a[c2].z; v[3] += a[c2].w; }
+                out_transform(v, p.svh + blk * kCols, lane);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    store_out(p.y, p.y_dtype, (int64_t) r * p.n + blk * kCols + lane * 4 + q, v[q]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ consumers
+        // input transform: one (128-block of k, row) per item; a block's
+        // fragments are ready when all its rows are
+        const int KB = p.k / kCols;
+        while (true) {
+            int item = 0;
+            if (lane == 0) item = (int) atomicAdd(&p.ctrl[3], 1u);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            if (item >= KB * rows) break;
+            const int r = item % rows;
+            item /= rows;
+            const int k0 = item * kCols + lane * 4;
+            {
+                float v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const __half a = load_act_half(p.x, p.x_dtype, (int64_t) r * p.k + k0 + q);
+                    v[q] = __half2float(__hmul(a, p.suh[k0 + q]));
+                }
+                wht128_warp(v, lane);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int kl = lane * 4 + q;
+                    const int ks = item * 8 + (kl >> 4);
+                    store_frag<PRECISE>(p.xg + ((size_t) ks * rows + r) * 4 * FW, kl & 15,
+                                        __float2half_rn(v[q] * kHadNorm));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                fence_proxy_async_global();
+                atom_add_release_gpu(&readyP[item / (p.kc / kCols)], 1u);
+            }
+        }
+        uint32_t it = 0, du = 0, uu = 0;
+        const int t4 = lane & 3, gr = lane >> 2;
+        const int RB = row_blocks(rows);
+        const int nst = p.kc / (16 * kStageSK);
+        while (true) {
+            const int slot = du % kLinDQ;
+            if (!mbar_wait_lanes(&S.dqf[slot], (du / kLinDQ) & 1u, status)) break;
+            const int valid = S.desc[slot][0];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.dqe[slot]);
+            ++du;
+            if (!valid) break;
             float acc[4][4];
 #pragma unroll
             for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-            bool ok = true;
-            for (int ks0 = 0; ks0 < kslices && ok; ks0 += sub) {
-                const int nks = min(sub, kslices - ks0);
-                if (ks0 > 0) consumers_sync();
-                build_bfrag<PRECISE>(S.bfrag, RB, p.rows, S.rows, p.x, p.x_dtype, p.k, s * kslices + ks0, nks,
-                                     p.suh, warp, lane);
-                consumers_sync();
-                const int n_st = nks / C::SK;
-                switch (RB) {
-                    case 1: ok = lin_consume<K, CB, 1, PRECISE>(S, it, n_st, acc, geom, warp, lane, status); break;
-                    case 2: ok = lin_consume<K, CB, 2, PRECISE>(S, it, n_st, acc, geom, warp, lane, status); break;
-                    case 3: ok = lin_consume<K, CB, 3, PRECISE>(S, it, n_st, acc, geom, warp, lane, status); break;
-                    default: ok = lin_consume<K, CB, 4, PRECISE>(S, it, n_st, acc, geom, warp, lane, status); break;
-                }
-                ok = consumers_all(ok);
-            }
-            if (!consumers_all(ok)) break;
-            acc_to_cbuf(S.cbuf, acc, RB, warp, lane);
-            consumers_sync();
-
-            bool finalize = true;
-            if (p.nchunks > 1) {
-                const int64_t col0 = (int64_t) j * kCols;
-                for (int idx = ctid; idx < p.rows * kCols; idx += kConsumerThreads) {
-                    const int r = idx / kCols, c = idx % kCols;
-                    p.partial[((int64_t) s * p.rows + r) * p.n + col0 + c] = S.cbuf[idx];
-                }
-                consumers_sync();
-                if (ctid == 0) {
-                    __threadfence();   // release: covers every consumer's writes (ordered by the barrier)
-                    const uint32_t old = atomicAdd(&p.colcnt[j], 1u);
-                    const int last = old == (uint32_t) (p.nchunks - 1);
-                    if (last) {
-                        atomicExch(&p.colcnt[j], 0u);
-                        __threadfence();   // acquire: the other chunks' partials
-                    }
-                    S.flag = last;
-                }
-                consumers_sync();
-                finalize = S.flag != 0;
-                if (finalize) {
-                    for (int idx = ctid; idx < p.rows * kCols; idx += kConsumerThreads) {
-                        const int r = idx / kCols, c = idx % kCols;
-                        float v = 0.f;
-                        for (int c2 = 0; c2 < p.nchunks; ++c2)
-                            v += __ldcg(&p.partial[((int64_t) c2 * p.rows + r) * p.n + col0 + c]);
-                        S.cbuf[idx] = v;
-                    }
-                    consumers_sync();
-                }
-            }
-            if (finalize) {
-                for (int r = warp; r < p.rows; r += kConsumerWarps) {
-                    float v[4];
+            if (!ring_consume_rb<K, CB, PRECISE>(RB, p.ring, ring, S.full, S.empty, it, nst, rows, acc, warp, lane,
+                                                 status)) break;
+            const int ps = (int) (uu & 1u);
+            if (!mbar_wait_lanes(&S.pempty[ps], ((uu >> 1) + 1u) & 1u, status)) break;
+            float* tile = ptile + (size_t) ps * rows * kCols;
+            const int col = warp * 16 + gr;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) v[q] = S.cbuf[r * kCols + lane * 4 + q];
-                    out_transform(v, p.svh + (int64_t) j * kCols, lane);
+            for (int rb = 0; rb < 4; ++rb)
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        store_out(p.y, p.y_dtype, (int64_t) r * p.n + (int64_t) j * kCols + lane * 4 + q, v[q]);
+                for (int h = 0; h < 2; ++h) {
+                    const int r = rb * 8 + 2 * t4 + h;
+                    if (r < rows) {
+                        tile[r * kCols + col] = acc[rb][h];
+                        tile[r * kCols + col + 8] = acc[rb][2 + h];
+                    }
                 }
-            }
-            consumers_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.pfull[ps]);
+            ++uu;
         }
     }
 
-    // Retire: the last CTA out restores the ticket counters for the next launch.
+    // Retire: the last CTA out restores the control words for the next launch.
     __syncthreads();
     if (tid == 0) {
         __threadfence();
         const uint32_t old = atomicAdd(&p.ctrl[1], 1u);
-        if (old == gridDim.x - 1) {
+        S.last_cta = old == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (S.last_cta) {
+        __threadfence();
+        for (int i = tid; i < p.nk; i += kLinThreads) readyP[i] = 0u;
+        if (tid == 0) {
             atomicExch(&p.ctrl[0], 0u);
+            atomicExch(&p.ctrl[3], 0u);
             atomicExch(&p.ctrl[1], 0u);
         }
     }
@@ -297,73 +381,102 @@ __global__ void __launch_bounds__(kThreads, 2) linear_kernel(LinearParams p) {
 // ------------------------------------------------------------------ host side
 namespace {
 
+struct LinPrepared {
+    bool ready = false;
+    int grid = 0;
+};
+std::mutex g_lin_mu;
+LinPrepared g_lin_prep[64][8][3][2];
+
 template <int K, int CB, bool PRECISE>
-int launch_linear(const LinearParams& p, int grid, cudaStream_t stream) {
+int launch_linear(const LinearParams& p, int units, int smem, cudaStream_t stream) {
     auto kern = linear_kernel<K, CB, PRECISE>;
-    const int smem = (int) sizeof(LinSmem<K>);
-    static std::once_flag once[64];
     int dev = 0;
     EXL3_CUDA(cudaGetDevice(&dev));
-    cudaError_t attr = cudaSuccess;
-    std::call_once(once[dev & 63], [&] {
-        attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    });
-    EXL3_CUDA(attr);
-    kern<<<grid, kThreads, smem, stream>>>(p);
+    EXL3_REQUIRE(dev < 64, EXL3_ERR_UNSUPPORTED, "device index >= 64");
+    int grid_max = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_lin_mu);
+        LinPrepared& pr = g_lin_prep[dev][K - 1][CB][PRECISE ? 1 : 0];
+        if (!pr.ready) {
+            DeviceInfo di;
+            if (int rc = device_info(dev, &di)) return rc;
+            const int smax = kLinHeadBytes + kLinRingBytes;
+            EXL3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+            int res = 0;
+            EXL3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, kern, kLinThreads, smax));
+            EXL3_REQUIRE(res > 0, EXL3_ERR_UNSUPPORTED, "linear kernel has no resident CTA");
+            pr.grid = di.sms * res;
+            pr.ready = true;
+        }
+        grid_max = pr.grid;
+    }
+    const int grid = units < grid_max ? units : grid_max;
+    kern<<<grid, kLinThreads, smem, stream>>>(p);
     EXL3_CUDA(cudaGetLastError());
     return EXL3_OK;
 }
 
 template <int K, bool PRECISE>
-int launch_linear_cb(int cb, const LinearParams& p, int grid, cudaStream_t s) {
+int launch_linear_cb(int cb, const LinearParams& p, int units, int smem, cudaStream_t s) {
     switch (cb) {
-        case 0: return launch_linear<K, 0, PRECISE>(p, grid, s);
-        case 1: return launch_linear<K, 1, PRECISE>(p, grid, s);
-        default: return launch_linear<K, 2, PRECISE>(p, grid, s);
+        case 0: return launch_linear<K, 0, PRECISE>(p, units, smem, s);
+        case 1: return launch_linear<K, 1, PRECISE>(p, units, smem, s);
+        default: return launch_linear<K, 2, PRECISE>(p, units, smem, s);
     }
 }
 
 template <bool PRECISE>
-int launch_linear_k(int K, int cb, const LinearParams& p, int grid, cudaStream_t s) {
+int launch_linear_k(int K, int cb, const LinearParams& p, int units, int smem, cudaStream_t s) {
     switch (K) {
-        case 1: return launch_linear_cb<1, PRECISE>(cb, p, grid, s);
-        case 2: return launch_linear_cb<2, PRECISE>(cb, p, grid, s);
-        case 3: return launch_linear_cb<3, PRECISE>(cb, p, grid, s);
-        case 4: return launch_linear_cb<4, PRECISE>(cb, p, grid, s);
-        case 5: return launch_linear_cb<5, PRECISE>(cb, p, grid, s);
-        case 6: return launch_linear_cb<6, PRECISE>(cb, p, grid, s);
-        case 7: return launch_linear_cb<7, PRECISE>(cb, p, grid, s);
-        default: return launch_linear_cb<8, PRECISE>(cb, p, grid, s);
+        case 1: return launch_linear_cb<1, PRECISE>(cb, p, units, smem, s);
+        case 2: return launch_linear_cb<2, PRECISE>(cb, p, units, smem, s);
+        case 3: return launch_linear_cb<3, PRECISE>(cb, p, units, smem, s);
+        case 4: return launch_linear_cb<4, PRECISE>(cb, p, units, smem, s);
+        case 5: return launch_linear_cb<5, PRECISE>(cb, p, units, smem, s);
+        case 6: return launch_linear_cb<6, PRECISE>(cb, p, units, smem, s);
+        case 7: return launch_linear_cb<7, PRECISE>(cb, p, units, smem, s);
+        default: return launch_linear_cb<8, PRECISE>(cb, p, units, smem, s);
     }
 }
 
-int launch_linear_any(int K, int cb, bool precise, const LinearParams& p, int grid, cudaStream_t s) {
-    return precise ? launch_linear_k<true>(K, cb, p, grid, s) : launch_linear_k<false>(K, cb, p, grid, s);
+int launch_linear_any(int K, int cb, bool precise, const LinearParams& p, int units, int smem, cudaStream_t s) {
+    return precise ? launch_linear_k<true>(K, cb, p, units, smem, s) : launch_linear_k<false>(K, cb, p, units, smem, s);
 }
 
-int stage_k(int K) { return stage_slices(K) * 16; }
-
-// k-chunk: a multiple of 128 and of the stage depth that divides k, chosen so
-// the unit count fills the grid about twice, between 256 and 1024 elements.
-int pick_kc(int64_t k, int64_t n, int K, int grid) {
-    const int64_t nbn = n / kCols;
-    const int step = stage_k(K) > 128 ? stage_k(K) : 128;
-    int best = -1;
-    for (int64_t kc = step; kc <= k; kc += step) {
-        if (k % kc) continue;
-        if (best < 0) best = (int) kc;
-        if (kc > 1024) break;
-        if (nbn * (k / kc) >= 2 * grid || kc <= 256) best = (int) kc;
+// k-chunks per 128-column block: the fewest (dividing k into whole 128-blocks,
+// at most kLinMaxChunks) that give every CTA of a full grid a unit.
+int pick_chunks(int64_t k, int64_t n, int grid) {
+    const int kb = (int) (k / 128);
+    const int64_t nb = n / 128;
+    int best = 1;
+    for (int c = 1; c <= kb && c <= kLinMaxChunks; ++c) {
+        if (kb % c) continue;
+        best = c;
+        if (nb * c >= (int64_t) grid) break;
     }
-    return best < 0 ? (int) k : best;
+    return best;
 }
 
-int64_t linear_chunks(int64_t k, int64_t n, int K, int grid) { return k / pick_kc(k, n, K, grid); }
-
-int grid_for(int device) {
+int assumed_grid() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
     DeviceInfo di;
-    if (device_info(device, &di) != EXL3_OK) return 0;
+    if (device_info(dev, &di) != EXL3_OK || di.sms <= 0) return 296;
     return di.sms * 2;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
 }
 
 template <int K, int CB>
@@ -432,20 +545,17 @@ extern "C" int exl3_dequant(const void* trellis, int64_t kt, int64_t nt, int K, 
     return EXL3_OK;
 }
 
-static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t n, int K, int grid) {
-    const int64_t chunks = linear_chunks(k, n, K, grid);
-    const int64_t part = chunks > 1 ? chunks * rows_blk * n * 4 : 0;
-    return EXL3_LINEAR_CTRL_BYTES + align_up(part, 256);
+// Scratch: control words, the input fragments (sized for 4-word fragments)
+// and the chunk partials.
+static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t n, int grid) {
+    const int nk = pick_chunks(k, n, grid);
+    return EXL3_LINEAR_CTRL_BYTES + align_up(k * rows_blk * 4, 256) + align_up((int64_t) nk * rows_blk * n * 4, 256);
 }
 
 extern "C" int64_t exl3_linear_scratch_bytes(int64_t rows, int64_t k, int64_t n, int K) {
     if (rows < 1 || k < 128 || n < 128 || K < 1 || K > 8) return -1;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-    int grid = grid_for(dev);
-    if (grid <= 0) grid = 296;
-    const int64_t rb = rows < kMaxRows ? rows : kMaxRows;
-    return linear_scratch_for(rb, k, n, K, grid);
+    const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
+    return linear_scratch_for(rb, k, n, assumed_grid());
 }
 
 extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis,
@@ -462,41 +572,55 @@ extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, 
                  "exl3_linear: dtype codes are 0 (fp16), 1 (bf16), 2 (fp32)");
     EXL3_REQUIRE(aligned16(trellis), EXL3_ERR_ARG, "exl3_linear: trellis must be 16-byte aligned");
     EXL3_REQUIRE(aligned16(scratch), EXL3_ERR_ARG, "exl3_linear: scratch must be 16-byte aligned");
-    int dev = 0;
-    EXL3_CUDA(cudaGetDevice(&dev));
-    const int grid_max = grid_for(dev);
-    EXL3_REQUIRE(grid_max > 0, EXL3_ERR_CUDA, "exl3_linear: cannot query the device");
-    const int64_t rb = rows < kMaxRows ? rows : kMaxRows;
-    const int64_t need = linear_scratch_for(rb, k, n, K, grid_max);
+    EXL3_REQUIRE(n / 128 + kLinOffCnt <= EXL3_LINEAR_CTRL_BYTES / 4,
+                 EXL3_ERR_UNSUPPORTED, "exl3_linear: n too large");
+    const int grid = assumed_grid();
+    const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
+    const int64_t need = linear_scratch_for(rb, k, n, grid);
     EXL3_REQUIRE(scratch_bytes >= need, EXL3_ERR_ARG, "exl3_linear: scratch too small (%lld < %lld bytes)",
                  (long long) scratch_bytes, (long long) need);
-    EXL3_REQUIRE(n / 128 + 16 <= EXL3_LINEAR_CTRL_BYTES / 4, EXL3_ERR_UNSUPPORTED, "exl3_linear: n too large");
+    auto encode = tmap_encoder();
+    EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "exl3_linear: cuTensorMapEncodeTiled is not available");
 
     LinearParams p{};
-    p.k = k;
-    p.n = n;
-    p.trellis = static_cast<const uint8_t*>(trellis);
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t) (16 * K), (cuuint64_t) (n / 16), (cuuint64_t) (k / 16)};
+        const cuuint64_t strides[2] = {(cuuint64_t) (32 * K), (cuuint64_t) (n / 16) * (cuuint64_t) (32 * K)};
+        const cuuint32_t box[3] = {(cuuint32_t) (16 * K), 8u, (cuuint32_t) kStageSK};
+        const cuuint32_t estr[3] = {1u, 1u, 1u};
+        const CUresult r = encode(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(trellis), dims,
+                                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        EXL3_REQUIRE(r == CUDA_SUCCESS, EXL3_ERR_CUDA, "exl3_linear: cuTensorMapEncodeTiled failed (%d)", (int) r);
+    }
+    p.k = (int) k;
+    p.n = (int) n;
     p.suh = static_cast<const __half*>(suh);
     p.svh = static_cast<const __half*>(svh);
     p.x_dtype = x_dtype;
     p.y_dtype = y_dtype;
-    p.kc = pick_kc(k, n, K, grid_max);
-    p.nchunks = (int) (k / p.kc);
-    EXL3_REQUIRE(p.kc % (stage_slices(K) * 16) == 0 && p.kc % 128 == 0 && k % p.kc == 0, EXL3_ERR_UNSUPPORTED,
-                 "exl3_linear: internal k-chunk %d does not tile k = %lld", p.kc, (long long) k);
+    p.nk = pick_chunks(k, n, grid);
+    p.kc = (int) (k / p.nk);
     uint8_t* sb = static_cast<uint8_t*>(scratch);
     p.ctrl = reinterpret_cast<uint32_t*>(sb);
-    p.colcnt = reinterpret_cast<uint32_t*>(sb) + 16;
-    p.partial = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES);
+    p.xg = reinterpret_cast<uint32_t*>(sb + EXL3_LINEAR_CTRL_BYTES);
+    p.partial = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES + align_up(k * rb * 4, 256));
+    const int fw = precise ? 2 : 4;
     const int esz_x = x_dtype == 2 ? 4 : 2, esz_y = y_dtype == 2 ? 4 : 2;
-    const int64_t units = (n / kCols) * p.nchunks;
-    const int grid = (int) (units < grid_max ? units : grid_max);
+    const int64_t units = (n / kCols) * p.nk;
     auto s = static_cast<cudaStream_t>(stream);
-    for (int64_t r0 = 0; r0 < rows; r0 += kMaxRows) {
-        p.rows = (int) ((rows - r0) < kMaxRows ? (rows - r0) : kMaxRows);
+    for (int64_t r0 = 0; r0 < rows; r0 += kLinMaxRows) {
+        p.rows = (int) ((rows - r0) < kLinMaxRows ? (rows - r0) : kLinMaxRows);
+        p.ring.wpart = kStageSK * 8 * 32 * K;
+        p.ring.slot_bytes = p.ring.wpart + kStageSK * p.rows * 16 * fw;
+        const int budget = kLinRingBytes - 2 * p.rows * kCols * 4;
+        const int nsl = budget / p.ring.slot_bytes;
+        p.ring.ns = nsl < 2 ? 2 : (nsl > kLinMaxStages ? kLinMaxStages : nsl);
+        const int smem = kLinHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * p.rows * kCols * 4;
+        EXL3_REQUIRE(smem <= kLinHeadBytes + kLinRingBytes, EXL3_ERR_UNSUPPORTED, "exl3_linear: stage too large");
         p.x = static_cast<const uint8_t*>(x) + r0 * k * esz_x;
         p.y = static_cast<uint8_t*>(y) + r0 * n * esz_y;
-        if (int rc = launch_linear_any(K, cb, precise != 0, p, grid, s)) return rc;
+        if (int rc = launch_linear_any(K, cb, precise != 0, p, (int) units, smem, s)) return rc;
     }
     return EXL3_OK;
 }

@@ -38,8 +38,8 @@
 #include <mutex>
 #include <utility>
 
-#include "engine.cuh"
 #include "host.hpp"
+#include "stage.cuh"
 
 namespace exl3 {
 
@@ -50,7 +50,7 @@ constexpr int kMoeMaxTopk = 16;
 constexpr int kMoeKmax = 4;          // weight part of a ring stage sized for K <= 4
 constexpr int kMoeMaxHidden = 8192;
 constexpr int kMoeMaxInter = 4096;
-constexpr int kMoeSK = 8;                                 // k-slices per ring stage
+constexpr int kMoeSK = kStageSK;                          // k-slices per ring stage
 constexpr int kMoeWBytes = kMoeSK * 8 * 32 * kMoeKmax;    // largest weight part of a stage (8 KB)
 constexpr int kMoeMaxStages = 12;                         // ring depth cap
 constexpr int kMoeRingBytes = 98304;                      // ring + partial tiles per CTA
@@ -109,17 +109,13 @@ static __device__ unsigned long long g_phase[PH_N];
 #define PHASE_MARK(c) do { const unsigned long long n_ = clock64(); ph_[c] += n_ - ph_t_; ph_t_ = n_; } while (0)
 #define PHASE_COUNT(c) (ph_[c] += 1)
 #define PHASE_FLUSH(lane) do { ph_[PH_TOTAL] = clock64() - ph_start_; if ((lane) == 0) for (int i_ = 0; i_ < PH_N; ++i_) atomicAdd(&g_phase[i_], ph_[i_]); } while (0)
-#define PH_PARAM , unsigned long long& ph_wait
 #define PH_ARG , ph_[PH_DATA]
-#define PH_FWD , ph_wait
 #else
 #define PHASE_DECL
 #define PHASE_MARK(c)
 #define PHASE_COUNT(c)
 #define PHASE_FLUSH(lane)
-#define PH_PARAM
 #define PH_ARG
-#define PH_FWD
 #endif
 
 // Tensor maps: one 3-D map per (projection kind, K) describes an expert
@@ -147,8 +143,7 @@ struct MoeParams {
     float limit;
     int kca, nka;               // gate/up k-chunk over H
     int kcb, nkb;               // down k-chunk over I
-    int slot_bytes, ns;         // ring: ns stages of slot_bytes (weights, then B fragments)
-    int wpart;                  // weight part of a stage: SK x 8 tiles x 32 * kmax bytes
+    RingGeom ring;              // ns stages of slot_bytes (weights: wpart bytes, then B fragments)
     uint32_t* ctrl;
     float* partA;               // [pairs][2][nka][I]
     uint32_t* xg;               // input fragments: per pair 2 * (H/16) row-slices of 16*FW bytes
@@ -252,109 +247,6 @@ struct alignas(128) MoeHead {
     alignas(128) CUtensorMap tmap;   // the producer's tensor map under construction
 };
 constexpr int kMoeHeadBytes = (int) ((sizeof(MoeHead) + 127) / 128 * 128);
-
-// B-fragment words per lane per row-slice: fast arithmetic keeps every
-// activation duplicated into both halves of a word (4 words: k = 2t, 2t+8,
-// 2t+1, 2t+9), the precise path packs pairs (2 words: (2t, 2t+1), (2t+8, 2t+9)).
-template <bool PRECISE> struct Frag { static constexpr int FW = PRECISE ? 2 : 4; };
-
-// Store one transformed activation (row-slice base `rs`, words) at in-slice
-// position kk (0..15) in the fragment layout of Frag<PRECISE>.
-template <bool PRECISE>
-__device__ __forceinline__ void store_frag(uint32_t* rs, int kk, __half h) {
-    const int t = (kk & 7) >> 1;
-    if constexpr (PRECISE) {
-        reinterpret_cast<__half*>(rs)[t * 4 + 2 * (kk >= 8 ? 1 : 0) + (kk & 1)] = h;
-    } else {
-        rs[t * 4 + ((kk & 1) ? 2 : 0) + (kk >= 8 ? 1 : 0)] = dup_half(h);
-    }
-}
-
-// Decode + MMA over `nst` ring stages of one unit; bit width K and row-block
-// count RB are compile-time so the inner loop carries no predicated MMAs.
-template <int K, int RB, int CB, bool PRECISE>
-__device__ __forceinline__ bool moe_consume(const MoeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                            uint32_t& it, int nst, int nrows, float (&acc)[4][4], int cwarp,
-                                            int lane, uint32_t* status PH_PARAM) {
-    using F = TileFmt<K>;
-    constexpr int FW = Frag<PRECISE>::FW;
-    constexpr int ROWW = 8 * F::WORDS;                 // words per k-slice row (8 tiles)
-    const LaneGeom<K> geom = lane_geom<K>(lane);
-    const int t4 = lane & 3, gr = lane >> 2;
-    int boff[RB];
-#pragma unroll
-    for (int rb = 0; rb < RB; ++rb) boff[rb] = min(rb * 8 + gr, nrows - 1) * 4 * FW + t4 * FW;
-    const int bstride = nrows * 4 * FW;                 // words per row-slice block of the unit
-    for (int st = 0; st < nst; ++st) {
-        const int slot = (int) (it % (uint32_t) p.ns);
-#ifdef EXL3_PHASE_CLOCK
-        const unsigned long long w0_ = clock64();
-#endif
-        if (!mbar_wait_lanes(&full[slot], (it / (uint32_t) p.ns) & 1u, status)) return false;
-#ifdef EXL3_PHASE_CLOCK
-        ph_wait += clock64() - w0_;
-#endif
-        const uint32_t* base = reinterpret_cast<const uint32_t*>(ring + (size_t) slot * p.slot_bytes);
-        const uint32_t* phi[F::NG];
-        const uint32_t* plo[F::NG];
-#pragma unroll
-        for (int h = 0; h < F::NG; ++h) {
-            phi[h] = base + cwarp * F::WORDS + geom.ihi[h];
-            plo[h] = base + cwarp * F::WORDS + geom.ilo[h];
-        }
-        const uint32_t* bf = base + p.wpart / 4;
-#pragma unroll
-        for (int i = 0; i < kMoeSK; ++i) {
-            uint32_t whi[F::NG], wlo[F::NG];
-#pragma unroll
-            for (int h = 0; h < F::NG; ++h) {
-                whi[h] = phi[h][i * ROWW];
-                wlo[h] = plo[h][i * ROWW];
-            }
-            uint32_t w[8], x[8];
-            tile_windows_w<K>(whi, wlo, geom, w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) x[j] = codebook_pair<CB>(w[j]);
-            const uint32_t* bs = bf + i * bstride;
-#pragma unroll
-            for (int rb = 0; rb < RB; ++rb) {
-                if constexpr (PRECISE) {
-                    mma_tile_precise(acc[rb], x, *reinterpret_cast<const uint2*>(bs + boff[rb]));
-                } else {
-                    mma_tile(acc[rb], x, *reinterpret_cast<const uint4*>(bs + boff[rb]));
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        ++it;
-    }
-    return true;
-}
-
-template <int K, int CB, bool PRECISE>
-__device__ __forceinline__ bool moe_consume_rb(int RB, const MoeParams& p, uint8_t* ring, uint64_t* full,
-                                               uint64_t* empty, uint32_t& it, int nst, int nrows, float (&acc)[4][4],
-                                               int cwarp, int lane, uint32_t* status PH_PARAM) {
-    switch (RB) {
-        case 1: return moe_consume<K, 1, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 2: return moe_consume<K, 2, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 3: return moe_consume<K, 3, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        default: return moe_consume<K, 4, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-    }
-}
-
-template <int CB, bool PRECISE>
-__device__ __forceinline__ bool moe_consume_any(int K, int RB, const MoeParams& p, uint8_t* ring, uint64_t* full,
-                                                uint64_t* empty, uint32_t& it, int nst, int nrows, float (&acc)[4][4],
-                                                int cwarp, int lane, uint32_t* status PH_PARAM) {
-    switch (K) {
-        case 1: return moe_consume_rb<1, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 2: return moe_consume_rb<2, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 3: return moe_consume_rb<3, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        default: return moe_consume_rb<4, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-    }
-}
 
 // Phase P: one warp transforms hidden block kb of every row of group g for
 // projection mat (0 gate, 1 up): fp16(x) * suh in fp16, 128-point Hadamard in
@@ -490,7 +382,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
     extern __shared__ __align__(128) uint8_t smem_raw[];
     MoeHead& S = *reinterpret_cast<MoeHead*>(smem_raw);
     uint8_t* ring = smem_raw + kMoeHeadBytes;
-    float* ptile = reinterpret_cast<float*>(ring + (size_t) p.ns * p.slot_bytes);   // [2][m][128]
+    float* ptile = reinterpret_cast<float*>(ring + (size_t) p.ring.ns * p.ring.slot_bytes);   // [2][m][128]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t* status = p.ctrl + 2;
     uint32_t* cntA = p.ctrl + kOffCntA;
@@ -500,7 +392,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
     uint32_t* cntG = p.ctrl + kOffCntG;
 
     if (tid == 0) {
-        for (int s = 0; s < p.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kMoeConsumerWarps); }
+        for (int s = 0; s < p.ring.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kMoeConsumerWarps); }
         for (int s = 0; s < kMoeDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], kMoeConsumerWarps + 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&S.pfull[s], kMoeConsumerWarps); mbar_init(&S.pempty[s], 1); }
         fence_barrier_init();
@@ -546,7 +438,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                     s = r % p.nkb;
                 }
                 int K = p.ktab ? p.ktab[P.gexp[g]] : p.kuni;
-                if (K < 1 || 256 * K * kMoeSK > p.wpart) K = 0;   // above the launch's kmax: stage too small
+                if (K < 1 || 256 * K * kMoeSK > p.ring.wpart) K = 0;   // above the launch's kmax: stage too small
                 d[0] = kind; d[1] = g; d[2] = mat; d[3] = blk; d[4] = s; d[5] = K;
             }
             if (lane == 0) {
@@ -614,16 +506,16 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             const uint32_t wbytes = (uint32_t) (kMoeSK * 8 * tb);
             const int bbytes = (int) (kMoeSK * rsb);
             for (int st = 0; st < nst && ok; ++st) {
-                const int slot = (int) (it % (uint32_t) p.ns);
+                const int slot = (int) (it % (uint32_t) p.ring.ns);
                 if (lane == 0) {
-                    ok = mbar_wait(&S.empty[slot], ((it / (uint32_t) p.ns) + 1u) & 1u, status);
+                    ok = mbar_wait(&S.empty[slot], ((it / (uint32_t) p.ring.ns) + 1u) & 1u, status);
                     PHASE_MARK(PH_PROD_SLOT);
                     if (ok) {
-                        uint8_t* dst = ring + (size_t) slot * p.slot_bytes;
+                        uint8_t* dst = ring + (size_t) slot * p.ring.slot_bytes;
                         if (valid) {
                             mbar_arrive_expect_tx(&S.full[slot], wbytes + (uint32_t) bbytes);
                             tma_load_3d(dst, gtm, 0, blk * 8, ks0 + st * kMoeSK, &S.full[slot]);
-                            bulk_g2s(dst + p.wpart, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
+                            bulk_g2s(dst + p.ring.wpart, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
                         } else {
                             mbar_arrive(&S.full[slot]);
                         }
@@ -638,9 +530,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         }
         // no bulk copy may still be writing shared memory when the CTA retires
         if (lane == 0) {
-            const uint32_t first = it > (uint32_t) p.ns ? it - (uint32_t) p.ns : 0u;
+            const uint32_t first = it > (uint32_t) p.ring.ns ? it - (uint32_t) p.ring.ns : 0u;
             for (uint32_t i = first; i < it; ++i)
-                if (!mbar_wait(&S.full[i % p.ns], (i / p.ns) & 1u, status)) break;
+                if (!mbar_wait(&S.full[i % p.ring.ns], (i / p.ring.ns) & 1u, status)) break;
         }
         PHASE_FLUSH(lane);
     } else if (warp == kMoeEpilogueWarp) {
@@ -754,7 +646,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-            const bool ok = moe_consume_any<CB, PRECISE>(K, row_blocks(nrows), p, ring, S.full, S.empty, it, nst,
+            const bool ok = ring_consume_any<CB, PRECISE>(K, row_blocks(nrows), p.ring, ring, S.full, S.empty, it, nst,
                                                          nrows, acc, warp, lane, status PH_ARG);
             PHASE_MARK(PH_UNIT);
             PHASE_COUNT(PH_UNITS);
@@ -1087,9 +979,9 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     // With a single k-chunk over I a block's partial is its full sum: the
     // epilogue reads it and writes the transformed value in place.
     p.partB = g.nkb > 1 ? reinterpret_cast<float*>(sb + g.off_partB) : p.downc;
-    ring_geom(m, k_table ? kmax : K, precise != 0, &p.wpart, &p.slot_bytes, &p.ns);
+    ring_geom(m, k_table ? kmax : K, precise != 0, &p.ring.wpart, &p.ring.slot_bytes, &p.ring.ns);
 
-    const int smem = kMoeHeadBytes + p.ns * p.slot_bytes + 2 * (int) m * kCols * 4;
+    const int smem = kMoeHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * (int) m * kCols * 4;
     auto s = static_cast<cudaStream_t>(stream);
     if (precise) {
         switch (cb) {
