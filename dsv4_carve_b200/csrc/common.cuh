@@ -98,21 +98,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
-// Warp-uniform bounded wait: lane 0 polls under the time bound, the verdict is
-// broadcast, then every lane observes the completed phase itself (one
-// try_wait that succeeds at once: the phase cannot advance again before this
-// warp releases the slot) so each lane gets the barrier's acquire ordering.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* status, int lane) {
-    bool ok = true;
-    if (lane == 0) ok = mbar_wait(bar, parity, status);
-    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    if (ok) {
-        for (int i = 0; i < 1024; ++i)
-            if (mbar_try_wait(bar, parity)) break;
-    }
-    return ok;
-}
-
 // Bounded wait polled by every lane of a warp (each lane gets the barrier's
 // acquire ordering itself); the verdict is made warp-uniform.
 __device__ __forceinline__ bool mbar_wait_lanes(uint64_t* bar, uint32_t parity, uint32_t* status) {
@@ -170,21 +155,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
-}
-
-// Named barrier over the consumer warps only (the producer warp never joins).
-__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
-    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
-}
-
-// Named barrier that also ANDs a predicate over the participating threads,
-// so a give-up decision is taken by all of them together.
-__device__ __forceinline__ bool named_all(uint32_t id, uint32_t threads, bool v) {
-    uint32_t r;
-    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-                 "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-                 : "=r"(r) : "r"((uint32_t) v), "r"(id), "r"(threads) : "memory");
-    return r != 0;
 }
 
 // ---------------------------------------------------------------- memory
