@@ -337,8 +337,11 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+#ifdef EXL3_PHASE_CLOCK
+            unsigned long long ph_wait = 0;   // the dense kernel records no phases
+#endif
             if (!ring_consume_rb<K, CB, PRECISE>(RB, p.ring, ring, S.full, S.empty, it, nst, rows, acc, warp, lane,
-                                                 status)) break;
+                                                 status PH_FWD)) break;
             const int ps = (int) (uu & 1u);
             if (!mbar_wait_lanes(&S.pempty[ps], ((uu >> 1) + 1u) & 1u, status)) break;
             float* tile = ptile + (size_t) ps * rows * kCols;
