@@ -382,6 +382,12 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------ host side
+// Tensor-core path for >= 64 rows (tc.cu).
+int64_t linear_tc_scratch_bytes(int64_t rows, int64_t k);
+bool linear_tc_eligible(int64_t rows, int64_t k, int64_t n);
+int linear_tc(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis, int K, int cb,
+              const void* suh, const void* svh, void* y, int y_dtype, void* scratch, cudaStream_t s);
+
 namespace {
 
 struct LinPrepared {
@@ -555,10 +561,16 @@ static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t n, int gr
     return EXL3_LINEAR_CTRL_BYTES + align_up(k * rows_blk * 4, 256) + align_up((int64_t) nk * rows_blk * n * 4, 256);
 }
 
+// Scratch for `rows` rows: the tensor-core path's (>= 64 rows) or the GEMV path's.
+static int64_t linear_need(int64_t rows, int64_t k, int64_t n, int grid) {
+    if (linear_tc_eligible(rows, k, n)) return linear_tc_scratch_bytes(rows, k);
+    const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
+    return linear_scratch_for(rb, k, n, grid);
+}
+
 extern "C" int64_t exl3_linear_scratch_bytes(int64_t rows, int64_t k, int64_t n, int K) {
     if (rows < 1 || k < 128 || n < 128 || K < 1 || K > 8) return -1;
-    const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
-    return linear_scratch_for(rb, k, n, assumed_grid());
+    return linear_need(rows, k, n, assumed_grid());
 }
 
 extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis,
@@ -579,9 +591,12 @@ extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, 
                  EXL3_ERR_UNSUPPORTED, "exl3_linear: n too large");
     const int grid = assumed_grid();
     const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
-    const int64_t need = linear_scratch_for(rb, k, n, grid);
+    const int64_t need = linear_need(rows, k, n, grid);
     EXL3_REQUIRE(scratch_bytes >= need, EXL3_ERR_ARG, "exl3_linear: scratch too small (%lld < %lld bytes)",
                  (long long) scratch_bytes, (long long) need);
+    if (linear_tc_eligible(rows, k, n))
+        return linear_tc(x, x_dtype, rows, k, n, trellis, K, cb, suh, svh, y, y_dtype, scratch,
+                         static_cast<cudaStream_t>(stream));
     auto encode = tmap_encoder();
     EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "exl3_linear: cuTensorMapEncodeTiled is not available");
 

@@ -135,3 +135,19 @@ def test_status_word_clean(cuda):
     _lib.call("exl3_scratch_status", scratch.data_ptr(), 0, 0, ctypes.addressof(word),
               torch.cuda.current_stream().cuda_stream)
     assert word.value == 0
+
+
+@pytest.mark.parametrize("rows", [64, 130, 256])
+@pytest.mark.parametrize("K,cb", [(2, 1), (6, 0)])
+def test_tensor_core_rows(cuda, oracle, rows, K, cb):
+    """64 rows or more go through the tcgen05 path (weights rounded to fp16 as
+    the reference decodes them, fp32 accumulation in tensor memory); 130 rows
+    leave a partial 128-row tile."""
+    got, want = _run(cuda, oracle, 1024, 512, K, cb, rows, True, seed=rows)
+    assert max_abs(got, want) <= TOL
+
+
+def test_tensor_core_config1_shape(cuda, oracle):
+    """A prefill-sized block through the tensor cores at the config-1 shape."""
+    got, want = _run(cuda, oracle, 4096, 4096, 6, 0, 128, True)
+    assert max_abs(got, want) <= TOL
