@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
 
 // ------------------------------------------------------------------ host side
 // Tensor-core path for >= 64 rows (tc.cu).
-int64_t linear_tc_scratch_bytes(int64_t rows, int64_t k);
+int64_t linear_tc_scratch_bytes(int64_t rows, int64_t k, int64_t n);
 bool linear_tc_eligible(int64_t rows, int64_t k, int64_t n);
 int linear_tc(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis, int K, int cb,
               const void* suh, const void* svh, void* y, int y_dtype, void* scratch, cudaStream_t s);
@@ -563,7 +563,7 @@ static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t n, int gr
 
 // Scratch for `rows` rows: the tensor-core path's (>= 64 rows) or the GEMV path's.
 static int64_t linear_need(int64_t rows, int64_t k, int64_t n, int grid) {
-    if (linear_tc_eligible(rows, k, n)) return linear_tc_scratch_bytes(rows, k);
+    if (linear_tc_eligible(rows, k, n)) return linear_tc_scratch_bytes(rows, k, n);
     const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
     return linear_scratch_for(rb, k, n, grid);
 }

@@ -137,14 +137,28 @@ def test_status_word_clean(cuda):
     assert word.value == 0
 
 
-@pytest.mark.parametrize("rows", [64, 130, 256])
+@pytest.mark.parametrize("rows", [64, 130, 256, 300, 512, 600])
 @pytest.mark.parametrize("K,cb", [(2, 1), (6, 0)])
 def test_tensor_core_rows(cuda, oracle, rows, K, cb):
     """64 rows or more go through the tcgen05 path (weights rounded to fp16 as
-    the reference decodes them, fp32 accumulation in tensor memory); 130 rows
-    leave a partial 128-row tile."""
+    the reference decodes them, fp32 accumulation in tensor memory).  130 and
+    300 rows end inside an MMA N block; 300 and 512 use the second
+    accumulator; 600 takes two 512-row passes."""
     got, want = _run(cuda, oracle, 1024, 512, K, cb, rows, True, seed=rows)
     assert max_abs(got, want) <= TOL
+
+
+def test_tensor_core_single_chunk_and_repeat(cuda, oracle):
+    """A 128-column, 256-k matrix is one strip of one k-chunk (no partial
+    sum); the split-k case (1024 x 512) run twice gives bitwise the same
+    result, so the strip counters are left zero between calls."""
+    got, want = _run(cuda, oracle, 256, 128, 4, 1, 96, True)
+    assert max_abs(got, want) <= TOL
+    w = synth.make_dense(1024, 512, 5, seed=8, cb=0).to(cuda)
+    x = synth.activations(200, 1024, seed=9, device=cuda)
+    a = ext.linear_forward(x, w.trellis, w.suh, w.svh, 5, 0, torch.float32)
+    b = ext.linear_forward(x, w.trellis, w.suh, w.svh, 5, 0, torch.float32)
+    assert torch.equal(a, b)
 
 
 def test_tensor_core_config1_shape(cuda, oracle):
