@@ -1,0 +1,849 @@
+// moe_tc.cu -- routed-expert MoE layer for prefill chunks (many rows per
+// expert) on the tcgen05 tensor cores.
+//
+// Replaces the fused prefill launch exl3_moe (orders/F1-ref/exl3_moe.cu:99-301,
+// orders/F1-ref/exl3_moe_kernel.cuh:17-283) together with the torch glue the
+// plugin runs around it (argsort / scatter_add counts / TEMP_ROWS_FUSED
+// slicing, recipe-lna/vllm_exl3_exl3.py.lna:1597-1704): the route plan is
+// built on the device.  Numerics are those of the decode layer
+// (recipe-lna/lna2/lna_moe_ticket.cu:5-12; semantic reference
+// recipe-lna/vllm_exl3_exl3.py.lna:988-1027): gate / up accumulate fp32 over
+// the fp16-rounded decoded weights, output Hadamard * svh in fp32,
+// silu(min(g, L)) * clamp(u, -L, L) -> fp16, * down suh, Hadamard -> fp16,
+// down fp32, output Hadamard * svh, per-token slot-order fp32 sum, one cast.
+//
+// Four launches per chunk of <= 2048 tokens, chained with programmatic
+// dependent launch:
+//  1. pf_plan_kernel (one CTA): per-expert token bitmasks -> counts -> pairs
+//     (expert, token) sorted by expert then token; slot -> pair; per-expert
+//     offsets of pairs, 128-row passes and work units; clears the counters.
+//  2. pf_input_kernel: every (pair, gate|up, 128-block of hidden): x -> fp16,
+//     * suh, Hadamard -> fp16 rows of xg / xu [pairs][hidden].
+//  3. pf_gemm_kernel (persistent, one CTA per SM): units from one ticket
+//     counter, all gate/up units (expert, 128-column strip of I, 128-row pass)
+//     before all down units (expert, 128-column strip of hidden, 128-row
+//     pass).  A down unit waits (bounded) until the 128-column strips of its
+//     pass are all written; those come only from gate/up units, claimed
+//     earlier and never waiting, so no co-residency is assumed.
+//       warp 16 (producer)  claims tickets, publishes unit descriptors, streams
+//                           per 64-k step the packed weights (bulk copies of
+//                           whole k-slice rows of 8 tiles) and the pass's
+//                           activation rows (2-D TMA, 128-byte swizzle);
+//       warps 0-15          decode the weight tiles, round to fp16 and write
+//                           them K-major / swizzled as the MMA's A operand;
+//       warp 17             owns 512 TMEM columns (two accumulator sets) and
+//                           issues tcgen05.mma: D[column][row] over the rows
+//                           of the pass (N = rows rounded to 16);
+//       warps 18-21         epilogue, overlapping the next unit's mainloop:
+//                           TMEM -> shared -> per row: gate/up: out-H * svh,
+//                           SwiGLU, * down suh, Hadamard -> fp16 down input;
+//                           down: out-H * svh -> fp32 down output rows.
+//  4. pf_gather_kernel: out[t] = sum over slots, in slot order, of
+//     weight * down output row of the slot's pair; one cast.
+// Every wait is bounded (2 s); a wait that runs out sets a status bit and the
+// roles wind down; TMEM is always freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "host.hpp"
+#include "tcgen05.cuh"
+
+namespace exl3 {
+
+constexpr int kPfDecWarps = 16;
+constexpr int kPfProducerWarp = 16;
+constexpr int kPfMmaWarp = 17;
+constexpr int kPfEpiWarp0 = 18;                 // warps 18..21: TMEM lane groups 2, 3, 0, 1
+constexpr int kPfEpiWarps = 4;
+constexpr int kPfThreads = (kPfEpiWarp0 + kPfEpiWarps) * 32;
+constexpr int kPfRows = 128;                    // rows per pass (MMA N <= 128)
+constexpr int kPfKStep = 64;                    // k per step (4 k-slices)
+constexpr int kPfKmax = 4;                      // largest bit width
+constexpr int kPfXBox = kPfRows * 128;          // one activation box [128 rows][64 k] fp16
+constexpr int kPfXStage = 2 * kPfXBox;          // gate + up boxes
+constexpr int kPfXStages = 3;
+constexpr int kPfAStage = 2 * 128 * 128;        // gate + up decoded tiles [128 cols][64 k] fp16
+constexpr int kPfAStages = 2;
+constexpr int kPfWStage = 2 * 4 * 8 * 32 * kPfKmax;   // 2 matrices x 4 k-slices x 8 tiles at K = 4
+constexpr int kPfWStages = 4;
+constexpr int kPfChunkRows = 32;                // epilogue staging rows
+constexpr int kPfStageBytes = 2 * kPfChunkRows * 128 * 4;
+constexpr int kPfDQ = 4;                        // unit descriptor queue depth
+constexpr int kPfMaxTokens = 2048;              // tokens per plan (TEMP_ROWS_FUSED)
+constexpr int kPfMaskWords = 16384;             // experts x token words of the plan's bitmasks
+constexpr int kPfMaxExperts = 1024;
+constexpr int kPfMaxTopk = 16;
+constexpr int kPfCtrlWords = 16;                // [0] ticket [2] status [4] gate/up units [5] down units [6] pairs
+constexpr int kPfCtrlBytes = 65536;             // control words + per-pass counters
+constexpr int kPfMaxPasses = kPfCtrlBytes / 4 - kPfCtrlWords;
+
+struct PfUnit {
+    int mode;        // 0 gate/up, 1 down, -1 end
+    int e;
+    int K;
+    int strip;
+    int row0;        // first pair of the pass
+    int rows;        // rows in the pass (1..128)
+    int gp;          // global pass index
+    int ksteps;
+};
+
+struct PfHead {
+    uint64_t wfull[kPfWStages], wempty[kPfWStages];
+    uint64_t aready[kPfAStages], afree[kPfAStages];
+    uint64_t xfull[kPfXStages], xfree[kPfXStages];
+    uint64_t accfull[2], accfree[2];
+    uint64_t dfull[kPfDQ], dempty[kPfDQ];
+    PfUnit desc[kPfDQ];
+    uint32_t tmem;
+};
+constexpr int kPfSmem = 1024 + kPfXStages * kPfXStage + kPfAStages * kPfAStage + kPfWStages * kPfWStage +
+                        kPfStageBytes + 512;
+static_assert(sizeof(PfHead) <= 512, "head must fit its slot");
+
+struct PfPlan {
+    int* e_off;      // [E + 1] first pair of each expert
+    int* pass_off;   // [E + 1] first global pass of each expert
+    int* gu_off;     // [E + 1] first gate/up unit of each expert
+    int* dn_off;     // [E + 1] first down unit of each expert
+    int* pair_tok;   // [cap] token of each pair
+    int* pair_exp;   // [cap] expert of each pair
+    int* slot_pair;  // [T * topk] pair of each slot, -1 if skipped
+};
+
+struct PfParams {
+    CUtensorMap xg_map, xu_map, xd_map;   // [cap][H] / [cap][H] / [cap][I] fp16, box [64, 128], 128-byte swizzle
+    const int64_t* tab[9];
+    const int32_t* ktab;
+    int Kscalar;
+    int E, H, I;
+    float limit;
+    uint32_t* ctrl;
+    PfPlan plan;
+    __half* xd;
+    float* dn;
+    const void* dummy;                    // aligned source for copies of a misaligned weight pointer
+};
+
+__device__ __forceinline__ void named_bar(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
+}
+
+// Largest i in [0, n] with off[i] <= u (off ascending, off[0] = 0).
+__device__ __forceinline__ int upper_slot(const int* off, int n, int u) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldcg(off + mid) <= u) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ------------------------------------------------------------------ 1. plan
+// Exclusive block scan of one value per thread (1024 threads); returns the
+// prefix, writes the total to *total.
+__device__ int block_scan_1024(int v, int* warp_tot, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = warp_tot[lane];
+        int s = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        warp_tot[lane] = s - w;
+        if (lane == 31) *total = s;
+    }
+    __syncthreads();
+    const int r = x - v + warp_tot[warp];
+    __syncthreads();
+    return r;
+}
+
+// Route plan of one chunk (recipe-lna/lna2/lna_moe_ticket.cu:147-214 builds
+// the same kind of plan per CTA for decode; recipe-lna/vllm_exl3_exl3.py.lna:1617-1629
+// is the argsort / count glue it replaces).  Pairs are ordered by expert,
+// then token, so results do not depend on timing; an expert listed twice in
+// one token's slots is one pair used by both slots.
+__global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T, int topk, int E, int H, int I,
+                                                       uint32_t* ctrl, PfPlan plan) {
+    extern __shared__ uint32_t pf_mask[];   // [E][W]
+    __shared__ int warp_tot[32];
+    __shared__ int totals[4];
+    pdl_launch_dependents();
+    const int tid = threadIdx.x;
+    const int W = (T + 31) >> 5;
+    for (int i = tid; i < E * W; i += 1024) pf_mask[i] = 0u;
+    __syncthreads();
+    for (int q = tid; q < T * topk; q += 1024) {
+        const int e = ids[q], t = q / topk;
+        if (e >= 0 && e < E) atomicOr(&pf_mask[e * W + (t >> 5)], 1u << (t & 31));
+    }
+    __syncthreads();
+    // per expert: pairs, passes, units; E <= 1024 = one expert per thread
+    int c = 0;
+    if (tid < E)
+        for (int w = 0; w < W; ++w) c += __popc(pf_mask[tid * W + w]);
+    const int passes = (c + kPfRows - 1) / kPfRows;
+    const int o_pair = block_scan_1024(c, warp_tot, &totals[0]);
+    const int o_pass = block_scan_1024(passes, warp_tot, &totals[1]);
+    const int o_gu = block_scan_1024(passes * (I / 128), warp_tot, &totals[2]);
+    const int o_dn = block_scan_1024(passes * (H / 128), warp_tot, &totals[3]);
+    if (tid < E) {
+        plan.e_off[tid] = o_pair;
+        plan.pass_off[tid] = o_pass;
+        plan.gu_off[tid] = o_gu;
+        plan.dn_off[tid] = o_dn;
+    }
+    if (tid == 0) {
+        plan.e_off[E] = totals[0];
+        plan.pass_off[E] = totals[1];
+        plan.gu_off[E] = totals[2];
+        plan.dn_off[E] = totals[3];
+    }
+    __syncthreads();
+    // pairs: one (expert, token word) item per thread
+    for (int it = tid; it < E * W; it += 1024) {
+        const int e = it / W, w = it % W;
+        uint32_t m = pf_mask[it];
+        if (!m) continue;
+        int base = __ldcg(plan.e_off + e);
+        for (int w2 = 0; w2 < w; ++w2) base += __popc(pf_mask[e * W + w2]);
+        while (m) {
+            const int b = __ffs(m) - 1;
+            m &= m - 1;
+            plan.pair_tok[base] = w * 32 + b;
+            plan.pair_exp[base] = e;
+            ++base;
+        }
+    }
+    // slot -> pair
+    for (int q = tid; q < T * topk; q += 1024) {
+        const int e = ids[q], t = q / topk;
+        int pr = -1;
+        if (e >= 0 && e < E) {
+            const int w = t >> 5;
+            pr = __ldcg(plan.e_off + e) + __popc(pf_mask[e * W + w] & ((1u << (t & 31)) - 1u));
+            for (int w2 = 0; w2 < w; ++w2) pr += __popc(pf_mask[e * W + w2]);
+        }
+        plan.slot_pair[q] = pr;
+    }
+    // the GEMM's ticket and per-pass counters start at zero
+    const int npass = totals[1] < kPfMaxPasses ? totals[1] : kPfMaxPasses;
+    for (int i = tid; i < npass; i += 1024) ctrl[kPfCtrlWords + i] = 0u;
+    if (tid == 0) {
+        ctrl[0] = 0u;
+        ctrl[4] = (uint32_t) totals[2];
+        ctrl[5] = (uint32_t) totals[3];
+        ctrl[6] = (uint32_t) totals[0];
+        if (totals[1] > kPfMaxPasses) {
+            // more passes than counters: run no units (reported as a plan overflow)
+            ctrl[4] = 0u;
+            ctrl[5] = 0u;
+            atomicOr(&ctrl[2], ERR_PLAN);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ 2. input
+// One warp per (pair, gate|up, 128-block of hidden): fp16(x) * suh (fp16),
+// Hadamard in fp32, / sqrt(128), -> fp16 (recipe-lna/lna2/lna_moe_ticket.cu:119-144).
+__global__ void __launch_bounds__(256) pf_input_kernel(const void* x, int x_dtype, int H, int cap,
+                                                       const uint32_t* ctrl, const int* pair_tok, const int* pair_exp,
+                                                       const int64_t* gsuh_tab, const int64_t* usuh_tab,
+                                                       __half* xg, __half* xu) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int npairs = (int) __ldcg(ctrl + 6);
+    const int nkb = H / 128;
+    const int64_t items = (int64_t) npairs * nkb * 2;
+    for (int64_t it = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5); it < items; it += (int64_t) gridDim.x * 8) {
+        const int pr = (int) (it / (nkb * 2));
+        const int r = (int) (it % (nkb * 2));
+        const int mat = r / nkb, kb = r % nkb;
+        const int t = pair_tok[pr], e = pair_exp[pr];
+        const __half* suh = reinterpret_cast<const __half*>((mat ? usuh_tab : gsuh_tab)[e]);
+        const int64_t k0 = (int64_t) kb * 128 + lane * 4;
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            v[q] = __half2float(__hmul(load_act_half(x, x_dtype, (int64_t) t * H + k0 + q), suh[k0 + q]));
+        wht128_warp(v, lane);
+        __half2 h0 = __floats2half2_rn(v[0] * kHadNorm, v[1] * kHadNorm);
+        __half2 h1 = __floats2half2_rn(v[2] * kHadNorm, v[3] * kHadNorm);
+        uint2 o;
+        o.x = *reinterpret_cast<uint32_t*>(&h0);
+        o.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>((mat ? xu : xg) + (int64_t) pr * H + k0) = o;
+    }
+}
+
+// ------------------------------------------------------------------ 3. GEMM
+// Decoders: one unit's k-steps at bit width K.  Warp w decodes, per step,
+// gate/up: matrix w / 8, n-tile w % 8, k-slices 0..3; down: n-tile w % 8,
+// k-slices 2 (w / 8) .. +1.
+template <int K, int CB>
+__device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
+                               int warp, int lane, uint32_t* status) {
+    using F = TileFmt<K>;
+    const LaneGeom<K> geom = lane_geom<K>(lane);
+    const int t4 = lane & 3, g = lane >> 2;
+    const int ntile = warp & 7;
+    const int m = u.mode == 0 ? (warp >> 3) : 0;
+    const int i0 = u.mode == 0 ? 0 : (warp >> 3) * 2;
+    const int ni = u.mode == 0 ? 4 : 2;
+    const int c0 = ntile * 16 + g;
+    for (int s = 0; s < u.ksteps; ++s, ++gs) {
+        const int ws = gs % kPfWStages, as = gs % kPfAStages;
+        if (!mbar_wait_lanes(&H.wfull[ws], (gs / kPfWStages) & 1u, status)) return false;
+        if (!mbar_wait_lanes(&H.afree[as], ((gs / kPfAStages) + 1u) & 1u, status)) return false;
+        const uint32_t* wst = reinterpret_cast<const uint32_t*>(Wring + ws * kPfWStage);
+        uint8_t* A = Abuf + as * kPfAStage + m * (128 * 128);
+        for (int ii = 0; ii < ni; ++ii) {
+            const int i = i0 + ii;
+            const uint32_t* t = wst + ((m * 4 + i) * 8 + ntile) * F::WORDS;
+            uint32_t w[8], xv[8];
+            tile_windows<K>(t, geom, w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xv[j] = codebook_pair<CB>(w[j]);
+            const int kk = i * 16 + 2 * t4;
+            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0, kk)) = round_pair(xv[0], xv[1]);
+            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0, kk + 8)) = round_pair(xv[2], xv[3]);
+            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0 + 8, kk)) = round_pair(xv[4], xv[5]);
+            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0 + 8, kk + 8)) = round_pair(xv[6], xv[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&H.aready[as]);
+            mbar_arrive(&H.wempty[ws]);
+        }
+    }
+    return true;
+}
+
+template <int CB>
+__device__ bool pf_decode_dispatch(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
+                                   int warp, int lane, uint32_t* status) {
+    switch (u.K) {
+        case 1: return pf_decode_unit<1, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
+        case 2: return pf_decode_unit<2, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
+        case 3: return pf_decode_unit<3, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
+        default: return pf_decode_unit<4, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
+    }
+}
+
+// Unit of ticket `tk` (mode -1 once the tickets run out).
+__device__ PfUnit pf_unit_of(const PfParams& p, int tk) {
+    PfUnit u{};
+    const int ngu = (int) __ldcg(p.ctrl + 4), ndn = (int) __ldcg(p.ctrl + 5);
+    if (tk >= ngu + ndn) { u.mode = -1; return u; }
+    u.mode = tk < ngu ? 0 : 1;
+    const int v = u.mode == 0 ? tk : tk - ngu;
+    const int* off = u.mode == 0 ? p.plan.gu_off : p.plan.dn_off;
+    const int e = upper_slot(off, p.E, v);
+    const int pass0 = __ldcg(p.plan.pass_off + e), passes = __ldcg(p.plan.pass_off + e + 1) - pass0;
+    const int local = v - __ldcg(off + e);
+    const int pass = local % passes;
+    const int pair0 = __ldcg(p.plan.e_off + e), cnt = __ldcg(p.plan.e_off + e + 1) - pair0;
+    u.e = e;
+    u.strip = local / passes;
+    u.row0 = pair0 + pass * kPfRows;
+    u.rows = min(kPfRows, cnt - pass * kPfRows);
+    u.gp = pass0 + pass;
+    u.K = p.ktab ? p.ktab[e] : p.Kscalar;
+    u.ksteps = (u.mode == 0 ? p.H : p.I) / kPfKStep;
+    return u;
+}
+
+template <int CB>
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ PfParams p) {
+    extern __shared__ uint8_t pf_raw[];
+    uint8_t* base = pf_raw + ((1024u - (smem_u32(pf_raw) & 1023u)) & 1023u);
+    uint8_t* Xbuf = base;
+    uint8_t* Abuf = Xbuf + kPfXStages * kPfXStage;
+    uint8_t* Wring = Abuf + kPfAStages * kPfAStage;
+    float* Stg = reinterpret_cast<float*>(Wring + kPfWStages * kPfWStage);    // [2][32][128] fp32
+    PfHead& H = *reinterpret_cast<PfHead*>(reinterpret_cast<uint8_t*>(Stg) + kPfStageBytes);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t* status = p.ctrl + 2;
+
+    if (tid == 0) {
+        for (int s = 0; s < kPfWStages; ++s) { mbar_init(&H.wfull[s], 1); mbar_init(&H.wempty[s], kPfDecWarps); }
+        for (int s = 0; s < kPfAStages; ++s) { mbar_init(&H.aready[s], kPfDecWarps); mbar_init(&H.afree[s], 1); }
+        for (int s = 0; s < kPfXStages; ++s) { mbar_init(&H.xfull[s], 1); mbar_init(&H.xfree[s], 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&H.accfull[s], 1); mbar_init(&H.accfree[s], kPfEpiWarps); }
+        for (int s = 0; s < kPfDQ; ++s) {
+            mbar_init(&H.dfull[s], 1);
+            mbar_init(&H.dempty[s], kPfDecWarps + 1 + kPfEpiWarps);
+        }
+        fence_barrier_init();
+    }
+    if (warp == kPfMmaWarp) tmem_alloc(&H.tmem, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = H.tmem;
+
+    if (warp == kPfProducerWarp) {
+        // ------------------------------------------------------------ producer
+        pdl_wait();
+        if (lane == 0) {
+            uint32_t gs = 0, issued_w = 0, issued_x = 0;
+            bool ok = true;
+            for (uint32_t n = 0; ok; ++n) {
+                const int tk = (int) atomicAdd(p.ctrl, 1u);
+                PfUnit u = pf_unit_of(p, tk);
+                if (u.mode >= 0 && (u.K < 1 || u.K > kPfKmax)) {
+                    set_error(status, ERR_BAD_K);
+                    u.mode = -1;
+                }
+                const int d = n % kPfDQ;
+                ok = mbar_wait(&H.dempty[d], ((n / kPfDQ) + 1u) & 1u, status);
+                if (!ok) break;
+                H.desc[d] = u;
+                mbar_arrive(&H.dfull[d]);
+                if (u.mode < 0) break;
+                if (u.mode == 1) {
+                    // the down input of this pass: every 128-column strip of I written
+                    ok = wait_counter(p.ctrl + kPfCtrlWords + u.gp, (uint32_t) (p.I / 128), status);
+                    if (!ok) break;
+                    fence_proxy_async_global();
+                }
+                const int nm = u.mode == 0 ? 2 : 1;
+                const int ncols = u.mode == 0 ? p.I : p.H;
+                const int64_t tile_bytes = 32 * u.K;
+                const int64_t slice_bytes = (int64_t) (ncols / 16) * tile_bytes;
+                const uint32_t wbytes = (uint32_t) (nm * 4 * 8 * tile_bytes);
+                const uint8_t* tr[2];
+                for (int m = 0; m < nm; ++m) {
+                    const int ti = u.mode == 0 ? m * 3 : 6;
+                    tr[m] = reinterpret_cast<const uint8_t*>(p.tab[ti][u.e]);
+                    if (!aligned16_dev(tr[m])) {
+                        set_error(status, ERR_MISALIGNED);
+                        tr[m] = static_cast<const uint8_t*>(p.dummy);
+                    }
+                }
+                const CUtensorMap* xmap[2] = {u.mode == 0 ? &p.xg_map : &p.xd_map, &p.xu_map};
+                for (int s = 0; s < u.ksteps && ok; ++s, ++gs) {
+                    const int ws = gs % kPfWStages, xs = gs % kPfXStages;
+                    ok = mbar_wait(&H.wempty[ws], ((gs / kPfWStages) + 1u) & 1u, status);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&H.wfull[ws], wbytes);
+                    issued_w = gs + 1;
+                    for (int m = 0; m < nm; ++m)
+                        for (int i = 0; i < 4; ++i) {
+                            const uint8_t* src = tr[m] == p.dummy
+                                                     ? tr[m]
+                                                     : tr[m] + (int64_t) (s * 4 + i) * slice_bytes + u.strip * 8 * tile_bytes;
+                            bulk_g2s(Wring + ws * kPfWStage + (m * 4 + i) * 8 * tile_bytes, src,
+                                     (uint32_t) (8 * tile_bytes), &H.wfull[ws]);
+                        }
+                    ok = mbar_wait(&H.xfree[xs], ((gs / kPfXStages) + 1u) & 1u, status);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&H.xfull[xs], (uint32_t) (nm * kPfXBox));
+                    for (int m = 0; m < nm; ++m)
+                        tma_load_2d(Xbuf + xs * kPfXStage + m * kPfXBox, xmap[m], s * kPfKStep, u.row0, &H.xfull[xs]);
+                    issued_x = gs + 1;
+                }
+            }
+            // no copy may still be in flight when the CTA retires
+            for (uint32_t i = issued_w > kPfWStages ? issued_w - kPfWStages : 0; i < issued_w; ++i)
+                if (!mbar_wait(&H.wfull[i % kPfWStages], (i / kPfWStages) & 1u, status)) break;
+            for (uint32_t i = issued_x > kPfXStages ? issued_x - kPfXStages : 0; i < issued_x; ++i)
+                if (!mbar_wait(&H.xfull[i % kPfXStages], (i / kPfXStages) & 1u, status)) break;
+        }
+    } else if (warp == kPfMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t gs = 0;
+            bool ok = true;
+            for (uint32_t n = 0; ok; ++n) {
+                const int d = n % kPfDQ;
+                if (!mbar_wait(&H.dfull[d], (n / kPfDQ) & 1u, status)) break;
+                const PfUnit u = H.desc[d];
+                mbar_arrive(&H.dempty[d]);
+                if (u.mode < 0) break;
+                const int a = n & 1;
+                ok = mbar_wait(&H.accfree[a], ((n >> 1) + 1u) & 1u, status);
+                if (!ok) break;
+                tc_fence_after();
+                const int nm = u.mode == 0 ? 2 : 1;
+                const uint32_t idesc = idesc_f16(128, (u.rows + 15) & ~15);
+                const uint32_t acc0 = tmem + (uint32_t) (a * 256);
+                for (int s = 0; s < u.ksteps; ++s, ++gs) {
+                    const int as = gs % kPfAStages, xs = gs % kPfXStages;
+                    ok = mbar_wait(&H.xfull[xs], (gs / kPfXStages) & 1u, status) &&
+                         mbar_wait(&H.aready[as], (gs / kPfAStages) & 1u, status);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(Abuf + as * kPfAStage), x0 = smem_u32(Xbuf + xs * kPfXStage);
+#pragma unroll
+                    for (int kk = 0; kk < kPfKStep / 16; ++kk)
+                        for (int m = 0; m < nm; ++m)
+                            tc_mma(acc0 + m * 128, sdesc_sw128(a0 + m * (128 * 128) + kk * 32),
+                                   sdesc_sw128(x0 + m * kPfXBox + kk * 32), idesc, (s | kk) != 0);
+                    tc_commit(&H.afree[as]);
+                    tc_commit(&H.xfree[xs]);
+                }
+                tc_commit(&H.accfull[a]);
+            }
+        }
+    } else if (warp < kPfDecWarps) {
+        // ------------------------------------------------------------ decoders
+        uint32_t gs = 0;
+        for (uint32_t n = 0;; ++n) {
+            const int d = n % kPfDQ;
+            if (!mbar_wait_lanes(&H.dfull[d], (n / kPfDQ) & 1u, status)) break;
+            const PfUnit u = H.desc[d];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&H.dempty[d]);
+            if (u.mode < 0) break;
+            if (!pf_decode_dispatch<CB>(H, Abuf, Wring, u, gs, warp, lane, status)) break;
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int lg = warp & 3;               // TMEM lane group of this warp
+        const int ew = warp - kPfEpiWarp0;     // 0..3
+        float* SG = Stg;
+        float* SU = Stg + kPfChunkRows * 128;
+        for (uint32_t n = 0;; ++n) {
+            const int d = n % kPfDQ;
+            mbar_wait_lanes(&H.dfull[d], (n / kPfDQ) & 1u, status);
+            // the four warps take one verdict: a completed phase stays complete
+            // until these warps have released the slot
+            named_bar(1, kPfEpiWarps * 32);
+            if (!__all_sync(0xffffffffu, mbar_try_wait(&H.dfull[d], (n / kPfDQ) & 1u))) break;
+            const PfUnit u = H.desc[d];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&H.dempty[d]);
+            if (u.mode < 0) break;
+            const int a = n & 1;
+            const bool ok = mbar_wait_lanes(&H.accfull[a], (n >> 1) & 1u, status);
+            tc_fence_after();
+            const uint32_t tbase = tmem + ((uint32_t) (lg * 32) << 16) + (uint32_t) (a * 256);
+            const int col = lg * 32 + lane;
+            const int e = u.e;
+            for (int c0 = 0; c0 < u.rows; c0 += kPfChunkRows) {
+                {
+                    float v[32];
+                    tc_ld32(tbase + (uint32_t) c0, v);
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) SG[r * 128 + col] = v[r];
+                    if (u.mode == 0) {
+                        tc_ld32(tbase + 128u + (uint32_t) c0, v);
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) SU[r * 128 + col] = v[r];
+                    }
+                }
+                named_bar(1, kPfEpiWarps * 32);
+                for (int r = ew * 8; r < ew * 8 + 8; ++r) {
+                    const int row = c0 + r;
+                    if (row >= u.rows || !ok) break;
+                    const int64_t pr = u.row0 + row;
+                    float gv[4];
+                    *reinterpret_cast<float4*>(gv) = *reinterpret_cast<const float4*>(SG + r * 128 + lane * 4);
+                    if (u.mode == 0) {
+                        float uv[4];
+                        *reinterpret_cast<float4*>(uv) = *reinterpret_cast<const float4*>(SU + r * 128 + lane * 4);
+                        const __half* gsv = reinterpret_cast<const __half*>(p.tab[2][e]) + u.strip * 128;
+                        const __half* usv = reinterpret_cast<const __half*>(p.tab[5][e]) + u.strip * 128;
+                        const __half* dsu = reinterpret_cast<const __half*>(p.tab[7][e]) + u.strip * 128;
+                        out_transform(gv, gsv, lane);
+                        out_transform(uv, usv, lane);
+                        float dv[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            float gg = gv[q], uu = uv[q];
+                            if (gg > p.limit) gg = p.limit;
+                            if (uu < -p.limit) uu = -p.limit;
+                            if (uu > p.limit) uu = p.limit;
+                            const __half ah = __float2half_rn((gg / (1.0f + __expf(-gg))) * uu);
+                            dv[q] = __half2float(__hmul(ah, dsu[lane * 4 + q]));
+                        }
+                        wht128_warp(dv, lane);
+                        __half2 h0 = __floats2half2_rn(dv[0] * kHadNorm, dv[1] * kHadNorm);
+                        __half2 h1 = __floats2half2_rn(dv[2] * kHadNorm, dv[3] * kHadNorm);
+                        uint2 o;
+                        o.x = *reinterpret_cast<uint32_t*>(&h0);
+                        o.y = *reinterpret_cast<uint32_t*>(&h1);
+                        *reinterpret_cast<uint2*>(p.xd + pr * p.I + u.strip * 128 + lane * 4) = o;
+                    } else {
+                        const __half* dsv = reinterpret_cast<const __half*>(p.tab[8][e]) + u.strip * 128;
+                        out_transform(gv, dsv, lane);
+                        __stcg(reinterpret_cast<float4*>(p.dn + pr * p.H + u.strip * 128 + lane * 4),
+                               make_float4(gv[0], gv[1], gv[2], gv[3]));
+                    }
+                }
+                named_bar(1, kPfEpiWarps * 32);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&H.accfree[a]);
+            if (u.mode == 0) {
+                // release this strip of the pass's down input to the down units
+                fence_proxy_async_global();
+                __threadfence();
+                named_bar(1, kPfEpiWarps * 32);
+                if (ew == 0 && lane == 0) atom_add_release_gpu(p.ctrl + kPfCtrlWords + u.gp, 1u);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kPfMmaWarp) {
+        tc_fence_after();
+        tmem_free(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------ 4. gather
+// out[t][c] = sum over slots j, in slot order, of weights[t][j] * dn[pair][c]
+// (recipe-lna/lna2/lna_moe_ticket.cu:409-428), fp32, one cast.
+__global__ void __launch_bounds__(256) pf_gather_kernel(const float* dn, const int* slot_pair, const float* weights,
+                                                        int T, int topk, int H, void* out, int out_dtype) {
+    pdl_wait();
+    const int64_t n4 = (int64_t) T * (H / 4);
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t) gridDim.x * blockDim.x) {
+        const int t = (int) (i / (H / 4));
+        const int c = (int) (i % (H / 4)) * 4;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int j = 0; j < topk; ++j) {
+            const int pr = slot_pair[t * topk + j];
+            if (pr < 0) continue;
+            const float w = weights[t * topk + j];
+            const float4 d = __ldcg(reinterpret_cast<const float4*>(dn + (int64_t) pr * H + c));
+            v[0] += w * d.x; v[1] += w * d.y; v[2] += w * d.z; v[3] += w * d.w;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) store_out(out, out_dtype, (int64_t) t * H + c + q, v[q]);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 pf_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+template <typename... Args>
+cudaError_t pf_launch(void (*kern)(Args...), dim3 grid, dim3 block, int smem, cudaStream_t s, bool pdl,
+                      const std::decay_t<Args>&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = (size_t) smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Tokens per plan: at most 2048, and the bitmasks must fit shared memory.
+int64_t pf_chunk_tokens(int64_t E) {
+    int64_t t = (int64_t) kPfMaskWords / E * 32;
+    if (t > kPfMaxTokens) t = kPfMaxTokens;
+    return t;
+}
+
+struct PfGeom {
+    int64_t cap;                  // pair capacity of one chunk = chunk tokens x topk
+    int64_t off_plan, off_xg, off_xu, off_xd, off_dn, total;
+};
+
+PfGeom pf_geom(int64_t m, int64_t topk, int64_t H, int64_t I, int64_t E) {
+    PfGeom g{};
+    int64_t ct = pf_chunk_tokens(E);
+    if (m < ct) ct = m;
+    g.cap = ct * topk;
+    int64_t o = kPfCtrlBytes;
+    g.off_plan = o;
+    o += align_up((4 * (E + 1) + 2 * g.cap + g.cap) * 4, 256);
+    g.off_xg = o;
+    o += align_up(g.cap * H * 2, 256);
+    g.off_xu = o;
+    o += align_up(g.cap * H * 2, 256);
+    g.off_xd = o;
+    o += align_up(g.cap * I * 2, 256);
+    g.off_dn = o;
+    o += align_up(g.cap * H * 4, 256);
+    g.total = o;
+    return g;
+}
+
+template <int CB>
+int pf_set_attr() {
+    static std::once_flag once[64];
+    int dev = 0;
+    EXL3_CUDA(cudaGetDevice(&dev));
+    cudaError_t attr = cudaSuccess;
+    std::call_once(once[dev & 63], [&] {
+        attr = cudaFuncSetAttribute(pf_gemm_kernel<CB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+        if (attr == cudaSuccess)
+            attr = cudaFuncSetAttribute(pf_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfMaskWords * 4);
+    });
+    EXL3_CUDA(attr);
+    return EXL3_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t exl3_moe_prefill_scratch_bytes(int64_t m, int64_t topk, int64_t hidden, int64_t inter,
+                                                  int64_t n_experts) {
+    if (m < 1 || topk < 1 || topk > kPfMaxTopk || hidden < 128 || inter < 128 || n_experts < 1 ||
+        n_experts > kPfMaxExperts)
+        return -1;
+    return pf_geom(m, topk, hidden, inter, n_experts).total;
+}
+
+extern "C" int64_t exl3_moe_prefill_chunk_tokens(int64_t n_experts) {
+    if (n_experts < 1 || n_experts > kPfMaxExperts) return -1;
+    return pf_chunk_tokens(n_experts);
+}
+
+extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
+                                int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
+                                const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
+                                const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
+                                const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
+                                int cb, const int32_t* ids, const float* weights, int64_t topk, float swiglu_limit,
+                                void* scratch, int64_t scratch_bytes, void* stream) {
+    EXL3_REQUIRE(x && out && ids && weights && scratch, EXL3_ERR_ARG, "exl3_moe_prefill: null pointer argument");
+    EXL3_REQUIRE(gate_trellis && gate_suh && gate_svh && up_trellis && up_suh && up_svh && down_trellis &&
+                     down_suh && down_svh,
+                 EXL3_ERR_ARG, "exl3_moe_prefill: null pointer table");
+    EXL3_REQUIRE(m >= 1, EXL3_ERR_ARG, "exl3_moe_prefill: m must be >= 1");
+    EXL3_REQUIRE(hidden % 128 == 0 && inter % 128 == 0 && hidden > 0 && inter > 0, EXL3_ERR_ARG,
+                 "exl3_moe_prefill: hidden and inter must be positive multiples of 128");
+    EXL3_REQUIRE(n_experts >= 1 && n_experts <= kPfMaxExperts, EXL3_ERR_ARG,
+                 "exl3_moe_prefill: n_experts must be in 1..%d", kPfMaxExperts);
+    EXL3_REQUIRE(topk >= 1 && topk <= kPfMaxTopk, EXL3_ERR_ARG, "exl3_moe_prefill: topk must be in 1..%d",
+                 kPfMaxTopk);
+    EXL3_REQUIRE(kmax >= 1 && kmax <= kPfKmax, EXL3_ERR_ARG, "exl3_moe_prefill: kmax must be in 1..%d", kPfKmax);
+    EXL3_REQUIRE(k_table || (K >= 1 && K <= kmax), EXL3_ERR_ARG, "exl3_moe_prefill: K must be in 1..kmax");
+    EXL3_REQUIRE(cb >= 0 && cb <= 2, EXL3_ERR_ARG, "exl3_moe_prefill: codebook must be 0, 1 or 2");
+    EXL3_REQUIRE(x_dtype >= 0 && x_dtype <= 1 && out_dtype >= 0 && out_dtype <= 2, EXL3_ERR_ARG,
+                 "exl3_moe_prefill: x must be fp16/bf16, out fp16/bf16/fp32");
+    EXL3_REQUIRE(swiglu_limit > 0.f, EXL3_ERR_ARG, "exl3_moe_prefill: swiglu_limit must be > 0");
+    EXL3_REQUIRE(aligned16(scratch), EXL3_ERR_ARG, "exl3_moe_prefill: scratch must be 16-byte aligned");
+    const PfGeom g = pf_geom(m, topk, hidden, inter, n_experts);
+    EXL3_REQUIRE(scratch_bytes >= g.total, EXL3_ERR_ARG, "exl3_moe_prefill: scratch too small (%lld < %lld bytes)",
+                 (long long) scratch_bytes, (long long) g.total);
+    auto encode = pf_encoder();
+    EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "exl3_moe_prefill: cuTensorMapEncodeTiled is not available");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int dev = 0;
+    EXL3_CUDA(cudaGetDevice(&dev));
+    DeviceInfo di;
+    {
+        const int drc = device_info(dev, &di);
+        if (drc != EXL3_OK) return drc;
+    }
+    int rc = cb == 0 ? pf_set_attr<0>() : cb == 1 ? pf_set_attr<1>() : pf_set_attr<2>();
+    if (rc != EXL3_OK) return rc;
+
+    uint8_t* sb = static_cast<uint8_t*>(scratch);
+    PfParams p{};
+    {
+        const int64_t rows_cap = g.cap;
+        __half* bufs[3] = {reinterpret_cast<__half*>(sb + g.off_xg), reinterpret_cast<__half*>(sb + g.off_xu),
+                           reinterpret_cast<__half*>(sb + g.off_xd)};
+        const int64_t widths[3] = {hidden, hidden, inter};
+        CUtensorMap* maps[3] = {&p.xg_map, &p.xu_map, &p.xd_map};
+        for (int i = 0; i < 3; ++i) {
+            const cuuint64_t dims[2] = {(cuuint64_t) widths[i], (cuuint64_t) rows_cap};
+            const cuuint64_t strides[1] = {(cuuint64_t) widths[i] * 2};
+            const cuuint32_t box[2] = {(cuuint32_t) kPfKStep, (cuuint32_t) kPfRows};
+            const cuuint32_t estr[2] = {1u, 1u};
+            const CUresult r = encode(maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bufs[i], dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            EXL3_REQUIRE(r == CUDA_SUCCESS, EXL3_ERR_CUDA, "exl3_moe_prefill: activation tensor map failed (%d)",
+                         (int) r);
+        }
+    }
+    const int64_t* tabs[9] = {gate_trellis, gate_suh, gate_svh, up_trellis, up_suh, up_svh,
+                              down_trellis, down_suh, down_svh};
+    for (int i = 0; i < 9; ++i) p.tab[i] = tabs[i];
+    p.ktab = k_table;
+    p.Kscalar = K;
+    p.E = (int) n_experts;
+    p.H = (int) hidden;
+    p.I = (int) inter;
+    p.limit = swiglu_limit;
+    p.ctrl = reinterpret_cast<uint32_t*>(sb);
+    int* pl = reinterpret_cast<int*>(sb + g.off_plan);
+    const int64_t E1 = n_experts + 1;
+    p.plan.e_off = pl;
+    p.plan.pass_off = pl + E1;
+    p.plan.gu_off = pl + 2 * E1;
+    p.plan.dn_off = pl + 3 * E1;
+    p.plan.pair_tok = pl + 4 * E1;
+    p.plan.pair_exp = pl + 4 * E1 + g.cap;
+    p.plan.slot_pair = pl + 4 * E1 + 2 * g.cap;
+    p.xd = reinterpret_cast<__half*>(sb + g.off_xd);
+    p.dn = reinterpret_cast<float*>(sb + g.off_dn);
+    p.dummy = sb + g.off_xg;
+
+    // the status word reports this call
+    EXL3_CUDA(cudaMemsetAsync(p.ctrl + 2, 0, sizeof(uint32_t), s));
+    const int64_t ct = g.cap / topk;
+    const int xb = 2;   // fp16 or bf16
+    const int ob = out_dtype == 2 ? 4 : 2;
+    for (int64_t t0 = 0; t0 < m; t0 += ct) {
+        const int T = (int) (m - t0 < ct ? m - t0 : ct);
+        const void* xc = static_cast<const uint8_t*>(x) + t0 * hidden * xb;
+        void* oc = static_cast<uint8_t*>(out) + t0 * hidden * ob;
+        const int32_t* idc = ids + t0 * topk;
+        const float* wc = weights + t0 * topk;
+        const int W = (T + 31) / 32;
+        EXL3_CUDA(pf_launch(pf_plan_kernel, dim3(1), dim3(1024), (int) (n_experts * W * 4), s, false, idc, T,
+                            (int) topk, (int) n_experts, (int) hidden, (int) inter, p.ctrl, p.plan));
+        const int64_t items = (int64_t) T * topk * (hidden / 128) * 2;
+        int64_t ib = (items + 7) / 8;
+        if (ib > (int64_t) di.sms * 16) ib = (int64_t) di.sms * 16;
+        EXL3_CUDA(pf_launch(pf_input_kernel, dim3((unsigned) ib), dim3(256), 0, s, true, xc, x_dtype, (int) hidden,
+                            (int) g.cap, (const uint32_t*) p.ctrl, (const int*) p.plan.pair_tok,
+                            (const int*) p.plan.pair_exp, gate_suh, up_suh, reinterpret_cast<__half*>(sb + g.off_xg),
+                            reinterpret_cast<__half*>(sb + g.off_xu)));
+        switch (cb) {
+            case 0: EXL3_CUDA(pf_launch(pf_gemm_kernel<0>, dim3(di.sms), dim3(kPfThreads), kPfSmem, s, true, p)); break;
+            case 1: EXL3_CUDA(pf_launch(pf_gemm_kernel<1>, dim3(di.sms), dim3(kPfThreads), kPfSmem, s, true, p)); break;
+            default: EXL3_CUDA(pf_launch(pf_gemm_kernel<2>, dim3(di.sms), dim3(kPfThreads), kPfSmem, s, true, p)); break;
+        }
+        int64_t gb = ((int64_t) T * (hidden / 4) + 255) / 256;
+        if (gb > (int64_t) di.sms * 8) gb = (int64_t) di.sms * 8;
+        EXL3_CUDA(pf_launch(pf_gather_kernel, dim3((unsigned) gb), dim3(256), 0, s, true, (const float*) p.dn,
+                            (const int*) p.plan.slot_pair, wc, T, (int) topk, (int) hidden, oc, out_dtype));
+    }
+    return EXL3_OK;
+}
+
+}  // namespace exl3

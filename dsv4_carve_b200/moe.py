@@ -202,3 +202,42 @@ def apply_moe_decode(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor
         _ACTIVE_LOGGED = True
         logger.warning("B200 EXL3 MoE kernel ACTIVE")
     return out
+
+
+def apply_moe_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, state: MoeState,
+                      expert_map: torch.Tensor | None = None, limit: float = 10.0,
+                      out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None):
+    """The fused prefill branch of apply_exl3_experts (the reference calls
+    exllamav3_ext.exl3_moe after torch argsort / count glue,
+    recipe-lna/vllm_exl3_exl3.py.lna:1597-1704): one tensor-core layer per
+    chunk of tokens, route plan on the device.  Returns the [T, hidden]
+    output, or None when the call is declined."""
+    T = int(x2d.shape[0])
+    if (not x2d.is_cuda or x2d.dim() != 2 or T < 1 or int(x2d.shape[1]) != state.hidden
+            or int(ids.shape[-1]) > 16 or state.kmax > 4):
+        _decline(f"prefill geometry x={tuple(x2d.shape)} topk={int(ids.shape[-1])}")
+        return None
+    local = map_topk_to_local(ids, state.n_experts, expert_map).reshape(ids.shape)
+    safe_ids = local.to(torch.int32).contiguous()
+    route_w = weights.reshape(local.shape).to(torch.float32).contiguous()
+    x = x2d if x2d.dtype in (torch.float16, torch.bfloat16) else x2d.to(torch.float16)
+    x = x.contiguous()
+    scratch = _ext._prefill_scratch(x.device, _ext.lna2_moe_prefill_scratch_bytes(
+        T, int(ids.shape[-1]), state.hidden, state.inter, state.n_experts))
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    _ext.lna2_moe_prefill(x, out, *state.table_list(), safe_ids, route_w, state.kmax, float(limit), scratch,
+                          intermediate=state.inter, k_table=state.ktab, codebook=state.codebook)
+    _CALLS["b200"] += 1
+    return out
+
+
+def apply_moe(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, state: MoeState,
+              expert_map: torch.Tensor | None = None, limit: float = 10.0,
+              out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None):
+    """Decode kernel up to its row ceiling, tensor-core prefill above it
+    (the plugin's lna2 / fused-exl3_moe split, vllm_exl3_exl3.py.lna:1707-1779)."""
+    if int(x2d.shape[0]) <= _ext.lna2_moe_max_rows() and int(x2d.shape[0]) * int(ids.shape[-1]) <= 256:
+        return apply_moe_decode(x2d, ids, weights, state, expert_map, limit, out, out_dtype)
+    return apply_moe_prefill(x2d, ids, weights, state, expert_map, limit, out, out_dtype)
+

@@ -269,3 +269,139 @@ def lna2_moe_decode(x: torch.Tensor, out: torch.Tensor,
                   kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
                   scratch.data_ptr(), scratch.numel(), int(bool(precise)), _stream(x.device))
     return out
+
+
+# --------------------------------------------------------------------- prefill MoE
+def lna2_moe_prefill_scratch_bytes(rows: int, topk: int = 8, hidden: int = 4096, intermediate: int = 2048,
+                                   n_experts: int = 256) -> int:
+    """Scratch bytes of lna2_moe_prefill for calls of up to `rows` tokens.
+
+    Calls longer than lna2_moe_prefill_chunk_tokens(n_experts) run in chunks
+    and need no more than one chunk's scratch."""
+    return int(_lib.load().exl3_moe_prefill_scratch_bytes(int(rows), int(topk), int(hidden), int(intermediate),
+                                                          int(n_experts)))
+
+
+def lna2_moe_prefill_chunk_tokens(n_experts: int = 256) -> int:
+    """Tokens per device route plan (2048 = the reference's TEMP_ROWS_FUSED at
+    256 experts, recipe-lna/vllm_exl3_exl3.py.lna:57)."""
+    return int(_lib.load().exl3_moe_prefill_chunk_tokens(int(n_experts)))
+
+
+def lna2_moe_prefill(x: torch.Tensor, out: torch.Tensor,
+                     gate_trellis: torch.Tensor, gate_suh: torch.Tensor, gate_svh: torch.Tensor,
+                     up_trellis: torch.Tensor, up_suh: torch.Tensor, up_svh: torch.Tensor,
+                     down_trellis: torch.Tensor, down_suh: torch.Tensor, down_svh: torch.Tensor,
+                     expert_ids: torch.Tensor, routing_weights: torch.Tensor, K: int,
+                     swiglu_limit: float, scratch: torch.Tensor, *, intermediate: int = 256,
+                     k_table: torch.Tensor | None = None, codebook: int = 1) -> torch.Tensor:
+    """Routed-expert layer for prefill chunks on the tensor cores; writes and
+    returns `out`.  Same arguments and checks as lna2_moe_decode, any row
+    count; the weights enter the MMA rounded to fp16 (the reference's decoded
+    values)."""
+    _check(x.is_cuda and x.dtype in (torch.float16, torch.bfloat16),
+           "LNA2 input must be CUDA fp16 or bf16")
+    _check(x.dim() == 2 and x.size(1) % 128 == 0, "LNA2 input must be [m,hidden] with hidden % 128 == 0")
+    _check(x.size(0) >= 1, "LNA2 row count out of range (m >= 1)")
+    _check(x.is_contiguous(), "LNA2 input must be contiguous")
+    _check(out.is_cuda and out.device == x.device and out.shape == x.shape and out.is_contiguous(),
+           "LNA2 output must match x shape/device and be contiguous")
+    _check(out.dtype in (torch.float16, torch.bfloat16, torch.float32), "LNA2 output must be fp16/bf16/fp32")
+    topk = expert_ids.size(-1) if expert_ids.dim() == 2 else -1
+    _check(expert_ids.is_cuda and expert_ids.dtype == torch.int32 and expert_ids.is_contiguous()
+           and expert_ids.dim() == 2 and expert_ids.size(0) == x.size(0) and 1 <= topk <= 16,
+           "LNA2 expert_ids must be contiguous int32 [m,topk]")
+    _check(routing_weights.is_cuda and routing_weights.dtype == torch.float32
+           and routing_weights.is_contiguous() and routing_weights.shape == expert_ids.shape,
+           "LNA2 routing_weights must be contiguous fp32 [m,topk]")
+    tables = (gate_trellis, gate_suh, gate_svh, up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh)
+    n_experts = gate_trellis.numel()
+    _check(1 <= n_experts <= 1024, "LNA2 pointer table has invalid expert count")
+    for t in tables:
+        _check(t.is_cuda and t.device == x.device and t.dtype == torch.int64 and t.is_contiguous()
+               and t.numel() == n_experts, "LNA2 pointer tables must be contiguous CUDA int64 [experts]")
+    limit = float(swiglu_limit)
+    _check(limit > 0.0 and limit < float("inf"), "LNA2 requires a finite positive SwiGLU limit")
+    inter = int(intermediate)
+    need = lna2_moe_prefill_scratch_bytes(x.size(0), topk, x.size(1), inter, n_experts)
+    _check(scratch.is_cuda and scratch.device == x.device and scratch.dtype == torch.uint8
+           and scratch.is_contiguous() and scratch.numel() >= need, "LNA2 scratch too small")
+    if k_table is None:
+        bits = int(K)
+        _check(1 <= bits <= 4, "LNA2 supports K1..K4 in this build")
+        kt_ptr, kmax = None, bits
+    else:
+        _check(k_table.is_cuda and k_table.device == x.device and k_table.dtype == torch.int32
+               and k_table.is_contiguous() and k_table.numel() == n_experts,
+               "LNA2 k_table must be contiguous CUDA int32 [experts]")
+        kt_ptr, kmax = k_table.data_ptr(), int(K)
+        bits = kmax
+    with _on_device(x.device):
+        _lib.call("exl3_moe_prefill", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                  x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
+                  kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
+                  scratch.data_ptr(), scratch.numel(), _stream(x.device))
+    return out
+
+
+_PREFILL_SCRATCH: dict = {}
+
+
+def _prefill_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    """One scratch tensor per device, grown on demand (prefill is not captured)."""
+    key = (device.type, device.index)
+    buf = _PREFILL_SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _PREFILL_SCRATCH[key] = buf
+    return buf
+
+
+def exl3_moe(hidden_state, output_state, expert_count, token_sorted, weight_sorted,
+             temp_state_g, temp_state_u, temp_intermediate_g, temp_intermediate_u,
+             act_function, K_gate, K_up, K_down,
+             gate_ptrs_trellis, gate_ptrs_suh, gate_ptrs_svh,
+             up_ptrs_trellis, up_ptrs_suh, up_ptrs_svh,
+             down_ptrs_trellis, down_ptrs_suh, down_ptrs_svh,
+             gate_mcg, gate_mul1, up_mcg, up_mul1, down_mcg, down_mul1,
+             act_limit, num_active=-1):
+    """exllamav3_ext.exl3_moe with its positional signature and checks
+    (orders/F1-ref/exl3_moe.cu:99-210): output_state (fp32, [T, hidden]) +=
+    the routed experts' contribution of the sorted slots.  The sorted-slot
+    form (expert_count [E+1] int64, token_sorted / weight_sorted [T*topk];
+    slots of expert E are skipped) is turned back into per-token slots and
+    handed to lna2_moe_prefill; the temp buffers are not used (this build
+    keeps its own scratch)."""
+    _check(hidden_state.is_cuda and hidden_state.dtype == torch.float16 and hidden_state.dim() == 2,
+           "hidden_state must be CUDA fp16 [T, hidden]")
+    _check(output_state.dtype == torch.float32 and output_state.shape == hidden_state.shape,
+           "output_state must be fp32 with hidden_state's shape")
+    _check(expert_count.dtype == torch.int64 and expert_count.dim() == 1, "expert_count must be int64 [E+1]")
+    _check(token_sorted.dtype == torch.int64 and token_sorted.shape == weight_sorted.shape,
+           "token_sorted / weight_sorted must be [T*topk]")
+    _check(gate_mcg == up_mcg == down_mcg and gate_mul1 == up_mul1 == down_mul1,
+           "MoE kernel: gate/up/down must share the same codebook")
+    _check(gate_mcg != gate_mul1, "MoE kernel: Only mcg and mul1 codebooks are supported")
+    _check(K_gate == K_up == K_down, "MoE kernel: gate/up/down must share one bit width in this build")
+    if num_active == 0:
+        return
+    T, hidden = hidden_state.shape
+    n_experts = expert_count.numel() - 1
+    topk = token_sorted.numel() // T
+    _check(topk * T == token_sorted.numel(), "token_sorted must hold T*topk slots")
+    ends = torch.cumsum(expert_count, 0)
+    pos = torch.arange(token_sorted.numel(), device=token_sorted.device)
+    expert_of = torch.searchsorted(ends, pos, right=True)
+    order = torch.argsort(token_sorted, stable=True)
+    ids = expert_of[order].view(T, topk)
+    ids = torch.where(ids < n_experts, ids, torch.full_like(ids, -1)).to(torch.int32).contiguous()
+    w = weight_sorted[order].view(T, topk).to(torch.float32).contiguous()
+    inter = int(temp_intermediate_g.size(-1))
+    y = torch.empty((T, hidden), dtype=torch.float32, device=hidden_state.device)
+    scratch = _prefill_scratch(hidden_state.device,
+                               lna2_moe_prefill_scratch_bytes(T, topk, hidden, inter, n_experts))
+    lna2_moe_prefill(hidden_state.contiguous(), y, gate_ptrs_trellis, gate_ptrs_suh, gate_ptrs_svh,
+                     up_ptrs_trellis, up_ptrs_suh, up_ptrs_svh, down_ptrs_trellis, down_ptrs_suh, down_ptrs_svh,
+                     ids, w, int(K_gate), float(act_limit), scratch, intermediate=inter,
+                     codebook=2 if gate_mul1 else 1)
+    output_state.add_(y)

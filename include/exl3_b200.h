@@ -157,6 +157,33 @@ int exl3_moe_decode_noalloc(const void* x, int x_dtype, void* out, int out_dtype
                             const int32_t* ids, const float* weights, int64_t topk,
                             float swiglu_limit, int precise, void* stream);
 
+/* ------------------------------------------------------------------ prefill MoE
+ * The routed-expert layer of exl3_moe_decode for many rows (prefill chunks)
+ * on the tcgen05 tensor cores: same arguments and semantics (gate / up / down
+ * multiply the fp16-rounded decoded weights the reference returns, i.e. the
+ * precise arithmetic), any m >= 1.  The route plan (the argsort / count glue
+ * of the reference's prefill branch) is built on the device, and calls with
+ * more than exl3_moe_prefill_chunk_tokens(n_experts) tokens (2048 at 256
+ * experts, the reference's TEMP_ROWS_FUSED) are processed in chunks of that
+ * many tokens, one after another on `stream`.  Bits: K1..K4 (k_table or K).
+ * Replaces the fused prefill launch exllamav3_ext.exl3_moe
+ * (orders/F1-ref/exl3_moe.cu:99-301) and its plugin glue
+ * (recipe-lna/vllm_exl3_exl3.py.lna:1597-1704).
+ * `scratch`: >= exl3_moe_prefill_scratch_bytes(m, topk, hidden, inter,
+ * n_experts) bytes; nothing in it needs clearing.  One launch at a time per
+ * scratch buffer.  Its status word (exl3_scratch_status(scratch, 1, ...))
+ * reports the last call. */
+int64_t exl3_moe_prefill_scratch_bytes(int64_t m, int64_t topk, int64_t hidden, int64_t inter, int64_t n_experts);
+int64_t exl3_moe_prefill_chunk_tokens(int64_t n_experts);
+int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_dtype,
+                     int64_t m, int64_t hidden, int64_t inter,
+                     const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
+                     const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
+                     const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh,
+                     int64_t n_experts, const int32_t* k_table, int K, int kmax, int cb,
+                     const int32_t* ids, const float* weights, int64_t topk,
+                     float swiglu_limit, void* scratch, int64_t scratch_bytes, void* stream);
+
 /* Device status word of a scratch buffer (MoE or linear): bit 0 dependency
  * wait timed out, bit 1 misaligned trellis pointer, bit 2 bit width out of
  * range, bit 3 ring wait timed out, bit 4 route plan overflow.  Synchronizes

@@ -91,6 +91,42 @@ def test_moe_argument_checks():
     _err(call(scratch_bytes=1024), "scratch too small")
 
 
+def test_moe_prefill_argument_checks_and_sizes():
+    lib = _lib.load()
+    buf = (C.c_uint8 * 64)()
+    p = C.addressof(buf)
+    tabs = [p] * 9
+
+    def call(m=512, H=4096, I=256, E=256, ktab=None, K=2, kmax=2, cb=1, topk=8, limit=10.0,
+             scratch_bytes=1 << 40, x=p, tables=tabs, scratch=p, x_dtype=0):
+        return lib.exl3_moe_prefill(x, x_dtype, p, 0, m, H, I, *tables, E, ktab, K, kmax, cb, p, p, topk,
+                                    C.c_float(limit), scratch, scratch_bytes, None)
+
+    _err(call(x=None), "null pointer")
+    _err(call(tables=[p] * 8 + [None]), "null pointer table")
+    _err(call(m=0), "m must be")
+    _err(call(topk=17), "topk")
+    _err(call(E=0), "n_experts")
+    _err(call(E=1025), "n_experts")
+    _err(call(H=4000), "multiples of 128")
+    _err(call(kmax=5), "kmax")
+    _err(call(K=3, kmax=2), "K must be")
+    _err(call(cb=3), "codebook")
+    _err(call(x_dtype=2), "fp16/bf16")
+    _err(call(limit=0.0), "swiglu_limit")
+    _err(call(scratch=p + 4), "16-byte aligned")
+    _err(call(scratch_bytes=1024), "scratch too small")
+    # sizes: one chunk of at most 2048 tokens at 256 experts, 512 at 1024
+    assert lib.exl3_moe_prefill_chunk_tokens(256) == 2048
+    assert lib.exl3_moe_prefill_chunk_tokens(1024) == 512
+    assert lib.exl3_moe_prefill_chunk_tokens(0) == -1
+    a = lib.exl3_moe_prefill_scratch_bytes(512, 8, 4096, 2048, 256)
+    b = lib.exl3_moe_prefill_scratch_bytes(4096, 8, 4096, 2048, 256)
+    c = lib.exl3_moe_prefill_scratch_bytes(2048, 8, 4096, 2048, 256)
+    assert 0 < a < b and b == c
+    assert lib.exl3_moe_prefill_scratch_bytes(512, 17, 4096, 2048, 256) == -1
+
+
 def test_status_word_checks():
     lib = _lib.load()
     _err(lib.exl3_scratch_status(None, 1, 0, None, None), "null")
