@@ -45,8 +45,10 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "host.hpp"
 #include "tcgen05.cuh"
@@ -62,8 +64,10 @@ constexpr int kPfThreads = (kPfEpiWarp0 + kPfEpiWarps) * 32;
 constexpr int kPfRows = 128;                    // rows per pass (MMA N <= 128)
 constexpr int kPfKStep = 64;                    // k per step (4 k-slices)
 constexpr int kPfKmax = 4;                      // largest bit width
-constexpr int kPfXBox = kPfRows * 128;          // one activation box [128 rows][64 k] fp16
-constexpr int kPfXStage = 2 * kPfXBox;          // gate + up boxes
+constexpr int kPfBoxRows = 16;                 // rows per activation TMA box
+constexpr int kPfBoxBytes = kPfBoxRows * 128;   // [16 rows][64 k] fp16
+constexpr int kPfXBox = kPfRows * 128;          // one matrix's activation tile [128 rows][64 k] fp16
+constexpr int kPfXStage = 2 * kPfXBox;          // gate + up tiles
 constexpr int kPfXStages = 3;
 constexpr int kPfAStage = 2 * 128 * 128;        // gate + up decoded tiles [128 cols][64 k] fp16
 constexpr int kPfAStages = 2;
@@ -79,6 +83,9 @@ constexpr int kPfMaxTopk = 16;
 constexpr int kPfCtrlWords = 16;                // [0] ticket [2] status [4] gate/up units [5] down units [6] pairs
 constexpr int kPfCtrlBytes = 65536;             // control words + per-pass counters
 constexpr int kPfMaxPasses = kPfCtrlBytes / 4 - kPfCtrlWords;
+constexpr int kPfMapSlots = 6;                  // weight tensor maps per matrix per CTA, used in turn by units
+constexpr int kPfMaxGrid = 256;                 // CTAs the map slots are sized for
+constexpr int kPfHeadBytes = 1024;
 
 struct PfUnit {
     int mode;        // 0 gate/up, 1 down, -1 end
@@ -92,6 +99,7 @@ struct PfUnit {
 };
 
 struct PfHead {
+    CUtensorMap tmap[2];                        // staging of this unit's weight maps (128-byte aligned)
     uint64_t wfull[kPfWStages], wempty[kPfWStages];
     uint64_t aready[kPfAStages], afree[kPfAStages];
     uint64_t xfull[kPfXStages], xfree[kPfXStages];
@@ -101,8 +109,8 @@ struct PfHead {
     uint32_t tmem;
 };
 constexpr int kPfSmem = 1024 + kPfXStages * kPfXStage + kPfAStages * kPfAStage + kPfWStages * kPfWStage +
-                        kPfStageBytes + 512;
-static_assert(sizeof(PfHead) <= 512, "head must fit its slot");
+                        kPfStageBytes + kPfHeadBytes;
+static_assert(sizeof(PfHead) <= kPfHeadBytes, "head must fit its slot");
 
 struct PfPlan {
     int* e_off;      // [E + 1] first pair of each expert
@@ -112,10 +120,14 @@ struct PfPlan {
     int* pair_tok;   // [cap] token of each pair
     int* pair_exp;   // [cap] expert of each pair
     int* slot_pair;  // [T * topk] pair of each slot, -1 if skipped
+    int4* units;     // [unit cap] {expert, strip, first pair, rows | global pass << 8}: gate/up units, then down
+    int unit_cap;
 };
 
 struct PfParams {
-    CUtensorMap xg_map, xu_map, xd_map;   // [cap][H] / [cap][H] / [cap][I] fp16, box [64, 128], 128-byte swizzle
+    CUtensorMap xg_map, xu_map, xd_map;   // [cap][H] / [cap][H] / [cap][I] fp16, box [64, 16], 128-byte swizzle
+    CUtensorMap tmpl[8];                  // weight map templates [gate/up, down][K - 1], box [16K, 8, 4]
+    CUtensorMap* maps;                    // [grid][kPfMapSlots][2] global slots the producer points at experts
     const int64_t* tab[9];
     const int32_t* ktab;
     int Kscalar;
@@ -125,8 +137,40 @@ struct PfParams {
     PfPlan plan;
     __half* xd;
     float* dn;
-    const void* dummy;                    // aligned source for copies of a misaligned weight pointer
 };
+
+// Compile-gated phase clocks (-DEXL3_PHASE_CLOCK): each role adds the
+// cycles it spends in its waits into g_pf_phase; exl3_pf_phase_read copies
+// them out.  Release builds compile all of it away.
+#ifdef EXL3_PHASE_CLOCK
+enum {
+    PF_DEC_DESC, PF_DEC_W, PF_DEC_AFREE, PF_DEC_TOTAL,
+    PF_MMA_DESC, PF_MMA_ACCFREE, PF_MMA_X, PF_MMA_A, PF_MMA_TOTAL,
+    PF_PR_TICKET, PF_PR_DEMPTY, PF_PR_DEP, PF_PR_WEMPTY, PF_PR_XFREE, PF_PR_TOTAL,
+    PF_EP_DESC, PF_EP_ACC, PF_EP_TOTAL, PF_UNITS, PF_N
+};
+__device__ unsigned long long g_pf_phase[PF_N];
+struct PfClock {
+    unsigned long long v[PF_N];
+    unsigned long long t;
+};
+#define PFC_PARAM , PfClock& pfc
+#define PFC_FWD , pfc
+#define PFC_DECL PfClock pfc{}; pfc.t = clock64(); const unsigned long long pfc_start = pfc.t;
+#define PFC_RESET() (pfc.t = clock64())
+#define PFC_MARK(c) do { const unsigned long long n_ = clock64(); pfc.v[c] += n_ - pfc.t; pfc.t = n_; } while (0)
+#define PFC_COUNT(c) (pfc.v[c] += 1)
+#define PFC_FLUSH(total, lane) do { pfc.v[total] = clock64() - pfc_start; \
+    if ((lane) == 0) for (int i_ = 0; i_ < PF_N; ++i_) if (pfc.v[i_]) atomicAdd(&g_pf_phase[i_], pfc.v[i_]); } while (0)
+#else
+#define PFC_PARAM
+#define PFC_FWD
+#define PFC_DECL
+#define PFC_RESET()
+#define PFC_MARK(c)
+#define PFC_COUNT(c)
+#define PFC_FLUSH(total, lane)
+#endif
 
 __device__ __forceinline__ void named_bar(int id, int threads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
@@ -182,6 +226,7 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
     extern __shared__ uint32_t pf_mask[];   // [E][W]
     __shared__ int warp_tot[32];
     __shared__ int totals[4];
+    __shared__ int s_pair[kPfMaxExperts + 1], s_pass[kPfMaxExperts + 1];
     pdl_launch_dependents();
     const int tid = threadIdx.x;
     const int W = (T + 31) >> 5;
@@ -206,20 +251,41 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
         plan.pass_off[tid] = o_pass;
         plan.gu_off[tid] = o_gu;
         plan.dn_off[tid] = o_dn;
+        s_pair[tid] = o_pair;
+        s_pass[tid] = o_pass;
     }
     if (tid == 0) {
         plan.e_off[E] = totals[0];
         plan.pass_off[E] = totals[1];
         plan.gu_off[E] = totals[2];
         plan.dn_off[E] = totals[3];
+        s_pair[E] = totals[0];
+        s_pass[E] = totals[1];
     }
     __syncthreads();
+    // unit table: gate/up units (expert, strip, pass), then down units; one
+    // expert per thread, so each thread still holds its own unit offsets
+    if (totals[2] + totals[3] <= plan.unit_cap) {
+        for (int e = tid; e < E; e += 1024) {
+            const int pe = s_pair[e], ce = s_pair[e + 1] - pe;
+            const int pass0 = s_pass[e], np = s_pass[e + 1] - pass0;
+            for (int ph = 0; ph < 2; ++ph) {
+                const int strips = ph == 0 ? I / 128 : H / 128;
+                int4* dst = plan.units + (ph == 0 ? o_gu : totals[2] + o_dn);
+                for (int st = 0; st < strips; ++st)
+                    for (int ps = 0; ps < np; ++ps) {
+                        const int rows = min(kPfRows, ce - ps * kPfRows);
+                        dst[st * np + ps] = make_int4(e, st, pe + ps * kPfRows, rows | ((pass0 + ps) << 8));
+                    }
+            }
+        }
+    }
     // pairs: one (expert, token word) item per thread
     for (int it = tid; it < E * W; it += 1024) {
         const int e = it / W, w = it % W;
         uint32_t m = pf_mask[it];
         if (!m) continue;
-        int base = __ldcg(plan.e_off + e);
+        int base = s_pair[e];
         for (int w2 = 0; w2 < w; ++w2) base += __popc(pf_mask[e * W + w2]);
         while (m) {
             const int b = __ffs(m) - 1;
@@ -235,7 +301,7 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
         int pr = -1;
         if (e >= 0 && e < E) {
             const int w = t >> 5;
-            pr = __ldcg(plan.e_off + e) + __popc(pf_mask[e * W + w] & ((1u << (t & 31)) - 1u));
+            pr = s_pair[e] + __popc(pf_mask[e * W + w] & ((1u << (t & 31)) - 1u));
             for (int w2 = 0; w2 < w; ++w2) pr += __popc(pf_mask[e * W + w2]);
         }
         plan.slot_pair[q] = pr;
@@ -248,7 +314,7 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
         ctrl[4] = (uint32_t) totals[2];
         ctrl[5] = (uint32_t) totals[3];
         ctrl[6] = (uint32_t) totals[0];
-        if (totals[1] > kPfMaxPasses) {
+        if (totals[1] > kPfMaxPasses || totals[2] + totals[3] > plan.unit_cap) {
             // more passes than counters: run no units (reported as a plan overflow)
             ctrl[4] = 0u;
             ctrl[5] = 0u;
@@ -258,72 +324,108 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
 }
 
 // ------------------------------------------------------------------ 2. input
-// One warp per (pair, gate|up, 128-block of hidden): fp16(x) * suh (fp16),
-// Hadamard in fp32, / sqrt(128), -> fp16 (recipe-lna/lna2/lna_moe_ticket.cu:119-144).
-__global__ void __launch_bounds__(256) pf_input_kernel(const void* x, int x_dtype, int H, int cap,
-                                                       const uint32_t* ctrl, const int* pair_tok, const int* pair_exp,
+// Four consecutive activations of x (fp16 or bf16) as fp16, one 8-byte load.
+__device__ __forceinline__ void load4_act(const void* x, int dtype, int64_t i, __half (&h)[4]) {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(x) + i * 2);
+    if (dtype == 0) {
+        *reinterpret_cast<uint2*>(h) = v;
+    } else {
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) h[q] = __float2half_rn(__bfloat162float(b[q]));
+    }
+}
+
+// fp16 activations -> one transformed 128-block: fp16(x) * suh (fp16),
+// Hadamard in fp32, / sqrt(128), -> fp16, stored as 4 halves per lane.
+__device__ __forceinline__ void pf_transform_store(const __half (&xh)[4], const __half* suh, int64_t k0, __half* dst,
+                                                   int lane) {
+    __half sh[4];
+    if ((reinterpret_cast<uintptr_t>(suh) & 7u) == 0) {
+        *reinterpret_cast<uint2*>(sh) = *reinterpret_cast<const uint2*>(suh + k0);
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sh[q] = suh[k0 + q];
+    }
+    float v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = __half2float(__hmul(xh[q], sh[q]));
+    wht128_warp(v, lane);
+    __half2 h0 = __floats2half2_rn(v[0] * kHadNorm, v[1] * kHadNorm);
+    __half2 h1 = __floats2half2_rn(v[2] * kHadNorm, v[3] * kHadNorm);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    *reinterpret_cast<uint2*>(dst + k0) = o;
+}
+
+// One CTA per pair (grid-stride); warp w transforms the 128-blocks w, w + 8,
+// ... of the pair's token row for gate and up
+// (recipe-lna/lna2/lna_moe_ticket.cu:119-144).
+__global__ void __launch_bounds__(256) pf_input_kernel(const void* x, int x_dtype, int H, const uint32_t* ctrl,
+                                                       const int* pair_tok, const int* pair_exp,
                                                        const int64_t* gsuh_tab, const int64_t* usuh_tab,
                                                        __half* xg, __half* xu) {
     pdl_wait();
     pdl_launch_dependents();
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int npairs = (int) __ldcg(ctrl + 6);
-    const int nkb = H / 128;
-    const int64_t items = (int64_t) npairs * nkb * 2;
-    for (int64_t it = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5); it < items; it += (int64_t) gridDim.x * 8) {
-        const int pr = (int) (it / (nkb * 2));
-        const int r = (int) (it % (nkb * 2));
-        const int mat = r / nkb, kb = r % nkb;
+    for (int pr = blockIdx.x; pr < npairs; pr += gridDim.x) {
         const int t = pair_tok[pr], e = pair_exp[pr];
-        const __half* suh = reinterpret_cast<const __half*>((mat ? usuh_tab : gsuh_tab)[e]);
-        const int64_t k0 = (int64_t) kb * 128 + lane * 4;
-        float v[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            v[q] = __half2float(__hmul(load_act_half(x, x_dtype, (int64_t) t * H + k0 + q), suh[k0 + q]));
-        wht128_warp(v, lane);
-        __half2 h0 = __floats2half2_rn(v[0] * kHadNorm, v[1] * kHadNorm);
-        __half2 h1 = __floats2half2_rn(v[2] * kHadNorm, v[3] * kHadNorm);
-        uint2 o;
-        o.x = *reinterpret_cast<uint32_t*>(&h0);
-        o.y = *reinterpret_cast<uint32_t*>(&h1);
-        *reinterpret_cast<uint2*>((mat ? xu : xg) + (int64_t) pr * H + k0) = o;
+        const __half* gs = reinterpret_cast<const __half*>(gsuh_tab[e]);
+        const __half* us = reinterpret_cast<const __half*>(usuh_tab[e]);
+        for (int kb = warp; kb < H / 128; kb += 8) {
+            const int64_t k0 = (int64_t) kb * 128 + lane * 4;
+            __half xh[4];
+            load4_act(x, x_dtype, (int64_t) t * H + k0, xh);
+            pf_transform_store(xh, gs, k0, xg + (int64_t) pr * H, lane);
+            pf_transform_store(xh, us, k0, xu + (int64_t) pr * H, lane);
+        }
     }
 }
 
 // ------------------------------------------------------------------ 3. GEMM
 // Decoders: one unit's k-steps at bit width K.  Warp w decodes, per step,
-// gate/up: matrix w / 8, n-tile w % 8, k-slices 0..3; down: n-tile w % 8,
-// k-slices 2 (w / 8) .. +1.
-template <int K, int CB>
-__device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
-                               int warp, int lane, uint32_t* status) {
+// gate/up (MODE 0): matrix w / 8, n-tile w % 8, k-slices 0..3; down (MODE 1):
+// n-tile w % 8, k-slices 2 (w / 8) .. +1.  Each 16x16 tile leaves the
+// registers in the m16n8k16 fragment layout it was decoded in, as one
+// stmatrix.x4 into the K-major 128-byte-swizzled A tile (lane l gives the
+// address of row (l % 8) + 8 (l / 16), 8-element chunk (l / 8) % 2).
+template <int K, int CB, int MODE>
+__device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, int ksteps, uint32_t& gs, int warp,
+                               int lane, uint32_t* status PFC_PARAM) {
     using F = TileFmt<K>;
+    constexpr int NI = MODE == 0 ? 4 : 2;
     const LaneGeom<K> geom = lane_geom<K>(lane);
-    const int t4 = lane & 3, g = lane >> 2;
     const int ntile = warp & 7;
-    const int m = u.mode == 0 ? (warp >> 3) : 0;
-    const int i0 = u.mode == 0 ? 0 : (warp >> 3) * 2;
-    const int ni = u.mode == 0 ? 4 : 2;
-    const int c0 = ntile * 16 + g;
-    for (int s = 0; s < u.ksteps; ++s, ++gs) {
+    const int m = MODE == 0 ? (warp >> 3) : 0;
+    const int i0 = MODE == 0 ? 0 : (warp >> 3) * 2;
+    const int row = ntile * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+    uint32_t off[NI];
+#pragma unroll
+    for (int ii = 0; ii < NI; ++ii) {
+        const int chunk = (i0 + ii) * 2 + ((lane >> 3) & 1);
+        off[ii] = (uint32_t) (m * (128 * 128) + row * 128 + ((chunk ^ (row & 7)) << 4));
+    }
+    const uint32_t abase = smem_u32(Abuf);
+    for (int s = 0; s < ksteps; ++s, ++gs) {
         const int ws = gs % kPfWStages, as = gs % kPfAStages;
+        PFC_RESET();
         if (!mbar_wait_lanes(&H.wfull[ws], (gs / kPfWStages) & 1u, status)) return false;
+        PFC_MARK(PF_DEC_W);
         if (!mbar_wait_lanes(&H.afree[as], ((gs / kPfAStages) + 1u) & 1u, status)) return false;
+        PFC_MARK(PF_DEC_AFREE);
         const uint32_t* wst = reinterpret_cast<const uint32_t*>(Wring + ws * kPfWStage);
-        uint8_t* A = Abuf + as * kPfAStage + m * (128 * 128);
-        for (int ii = 0; ii < ni; ++ii) {
-            const int i = i0 + ii;
-            const uint32_t* t = wst + ((m * 4 + i) * 8 + ntile) * F::WORDS;
+        const uint32_t a = abase + (uint32_t) (as * kPfAStage);
+#pragma unroll
+        for (int ii = 0; ii < NI; ++ii) {
+            const uint32_t* t = wst + ((m * 4 + i0 + ii) * 8 + ntile) * F::WORDS;
             uint32_t w[8], xv[8];
             tile_windows<K>(t, geom, w);
 #pragma unroll
             for (int j = 0; j < 8; ++j) xv[j] = codebook_pair<CB>(w[j]);
-            const int kk = i * 16 + 2 * t4;
-            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0, kk)) = round_pair(xv[0], xv[1]);
-            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0, kk + 8)) = round_pair(xv[2], xv[3]);
-            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0 + 8, kk)) = round_pair(xv[4], xv[5]);
-            *reinterpret_cast<uint32_t*>(A + sw128_offset(c0 + 8, kk + 8)) = round_pair(xv[6], xv[7]);
+            stmatrix_x4(a + off[ii], round_pair(xv[0], xv[1]), round_pair(xv[2], xv[3]), round_pair(xv[4], xv[5]),
+                        round_pair(xv[6], xv[7]));
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -335,36 +437,37 @@ __device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, c
     return true;
 }
 
-template <int CB>
-__device__ bool pf_decode_dispatch(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
-                                   int warp, int lane, uint32_t* status) {
+template <int CB, int MODE>
+__device__ bool pf_decode_k(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs, int warp,
+                            int lane, uint32_t* status PFC_PARAM) {
     switch (u.K) {
-        case 1: return pf_decode_unit<1, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
-        case 2: return pf_decode_unit<2, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
-        case 3: return pf_decode_unit<3, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
-        default: return pf_decode_unit<4, CB>(H, Abuf, Wring, u, gs, warp, lane, status);
+        case 1: return pf_decode_unit<1, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
+        case 2: return pf_decode_unit<2, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
+        case 3: return pf_decode_unit<3, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
+        default: return pf_decode_unit<4, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
     }
 }
 
-// Unit of ticket `tk` (mode -1 once the tickets run out).
-__device__ PfUnit pf_unit_of(const PfParams& p, int tk) {
+template <int CB>
+__device__ bool pf_decode_dispatch(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
+                                   int warp, int lane, uint32_t* status PFC_PARAM) {
+    return u.mode == 0 ? pf_decode_k<CB, 0>(H, Abuf, Wring, u, gs, warp, lane, status PFC_FWD)
+                       : pf_decode_k<CB, 1>(H, Abuf, Wring, u, gs, warp, lane, status PFC_FWD);
+}
+
+// Unit of ticket `tk` (mode -1 once the tickets run out); ngu / ndn are
+// the gate/up and down unit counts.
+__device__ PfUnit pf_unit_of(const PfParams& p, int tk, int ngu, int ndn) {
     PfUnit u{};
-    const int ngu = (int) __ldcg(p.ctrl + 4), ndn = (int) __ldcg(p.ctrl + 5);
     if (tk >= ngu + ndn) { u.mode = -1; return u; }
+    const int4 r = __ldcg(p.plan.units + tk);
     u.mode = tk < ngu ? 0 : 1;
-    const int v = u.mode == 0 ? tk : tk - ngu;
-    const int* off = u.mode == 0 ? p.plan.gu_off : p.plan.dn_off;
-    const int e = upper_slot(off, p.E, v);
-    const int pass0 = __ldcg(p.plan.pass_off + e), passes = __ldcg(p.plan.pass_off + e + 1) - pass0;
-    const int local = v - __ldcg(off + e);
-    const int pass = local % passes;
-    const int pair0 = __ldcg(p.plan.e_off + e), cnt = __ldcg(p.plan.e_off + e + 1) - pair0;
-    u.e = e;
-    u.strip = local / passes;
-    u.row0 = pair0 + pass * kPfRows;
-    u.rows = min(kPfRows, cnt - pass * kPfRows);
-    u.gp = pass0 + pass;
-    u.K = p.ktab ? p.ktab[e] : p.Kscalar;
+    u.e = r.x;
+    u.strip = r.y;
+    u.row0 = r.z;
+    u.rows = r.w & 255;
+    u.gp = r.w >> 8;
+    u.K = p.ktab ? p.ktab[u.e] : p.Kscalar;
     u.ksteps = (u.mode == 0 ? p.H : p.I) / kPfKStep;
     return u;
 }
@@ -400,66 +503,101 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
 
     if (warp == kPfProducerWarp) {
         // ------------------------------------------------------------ producer
+        // Lane 0 claims tickets and issues the copies; the whole warp points
+        // the unit's weight tensor maps at the expert (tensormap.replace in
+        // shared memory, release to this CTA's global slot, acquire).  A slot
+        // is reused kPfMapSlots units later, after more weight stages than
+        // the ring holds have been issued, so no copy still reads it.
         pdl_wait();
-        if (lane == 0) {
-            uint32_t gs = 0, issued_w = 0, issued_x = 0;
-            bool ok = true;
-            for (uint32_t n = 0; ok; ++n) {
-                const int tk = (int) atomicAdd(p.ctrl, 1u);
-                PfUnit u = pf_unit_of(p, tk);
-                if (u.mode >= 0 && (u.K < 1 || u.K > kPfKmax)) {
-                    set_error(status, ERR_BAD_K);
-                    u.mode = -1;
-                }
-                const int d = n % kPfDQ;
+        uint32_t gs = 0, issued_w = 0, issued_x = 0;
+        bool ok = true;
+        const int ngu = (int) __ldcg(p.ctrl + 4), ndn = (int) __ldcg(p.ctrl + 5);
+        // the next ticket is claimed one unit ahead, so its latency overlaps
+        // the current unit's copies (tickets still rise per CTA, so a down
+        // unit never waits on a unit this CTA holds back)
+        int tk_next = 0;
+        if (lane == 0) tk_next = (int) atomicAdd(p.ctrl, 1u);
+        PFC_DECL
+        for (uint32_t n = 0; ok; ++n) {
+            const int tk = __shfl_sync(0xffffffffu, tk_next, 0);
+            PFC_RESET();
+            PfUnit u = pf_unit_of(p, tk, ngu, ndn);
+            if (u.mode >= 0 && lane == 0) tk_next = (int) atomicAdd(p.ctrl, 1u);
+            if (u.mode >= 0 && (u.K < 1 || u.K > kPfKmax)) {
+                if (lane == 0) set_error(status, ERR_BAD_K);
+                u.mode = -1;
+            }
+            PFC_MARK(PF_PR_TICKET);
+            const int d = n % kPfDQ;
+            if (lane == 0) {
                 ok = mbar_wait(&H.dempty[d], ((n / kPfDQ) + 1u) & 1u, status);
-                if (!ok) break;
-                H.desc[d] = u;
-                mbar_arrive(&H.dfull[d]);
-                if (u.mode < 0) break;
+                if (ok) {
+                    H.desc[d] = u;
+                    mbar_arrive(&H.dfull[d]);
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            PFC_MARK(PF_PR_DEMPTY);
+            if (!ok || u.mode < 0) break;
+            const int nm = u.mode == 0 ? 2 : 1;
+            // weight tensor maps of the unit's matrices
+            const CUtensorMap* wmap[2] = {nullptr, nullptr};
+            bool valid = true;
+            for (int m = 0; m < nm; ++m) {
+                const void* wp = reinterpret_cast<const void*>(p.tab[u.mode == 0 ? m * 3 : 6][u.e]);
+                if (!aligned16_dev(wp) || wp == nullptr) { valid = false; continue; }
+                CUtensorMap* gtm = p.maps + ((size_t) blockIdx.x * kPfMapSlots + n % kPfMapSlots) * 2 + m;
+                const uint4* tsrc = reinterpret_cast<const uint4*>(&p.tmpl[u.mode * 4 + u.K - 1]);
+                if (lane < 8) reinterpret_cast<uint4*>(&H.tmap[m])[lane] = tsrc[lane];
+                __syncwarp();
+                if (lane == 0) tmap_replace_address(&H.tmap[m], wp);
+                __syncwarp();
+                tmap_publish(gtm, &H.tmap[m]);
+                if (lane == 0) tmap_acquire(gtm);
+                wmap[m] = gtm;
+            }
+            if (!valid && lane == 0) set_error(status, ERR_MISALIGNED);
+            if (lane == 0) {
                 if (u.mode == 1) {
                     // the down input of this pass: every 128-column strip of I written
                     ok = wait_counter(p.ctrl + kPfCtrlWords + u.gp, (uint32_t) (p.I / 128), status);
-                    if (!ok) break;
                     fence_proxy_async_global();
                 }
-                const int nm = u.mode == 0 ? 2 : 1;
-                const int ncols = u.mode == 0 ? p.I : p.H;
-                const int64_t tile_bytes = 32 * u.K;
-                const int64_t slice_bytes = (int64_t) (ncols / 16) * tile_bytes;
-                const uint32_t wbytes = (uint32_t) (nm * 4 * 8 * tile_bytes);
-                const uint8_t* tr[2];
-                for (int m = 0; m < nm; ++m) {
-                    const int ti = u.mode == 0 ? m * 3 : 6;
-                    tr[m] = reinterpret_cast<const uint8_t*>(p.tab[ti][u.e]);
-                    if (!aligned16_dev(tr[m])) {
-                        set_error(status, ERR_MISALIGNED);
-                        tr[m] = static_cast<const uint8_t*>(p.dummy);
-                    }
-                }
+                PFC_MARK(PF_PR_DEP);
+                const uint32_t wbytes = (uint32_t) (nm * 4 * 8 * 32 * u.K);
                 const CUtensorMap* xmap[2] = {u.mode == 0 ? &p.xg_map : &p.xd_map, &p.xu_map};
+                const int nbox = (u.rows + kPfBoxRows - 1) / kPfBoxRows;
                 for (int s = 0; s < u.ksteps && ok; ++s, ++gs) {
                     const int ws = gs % kPfWStages, xs = gs % kPfXStages;
+                    PFC_RESET();
                     ok = mbar_wait(&H.wempty[ws], ((gs / kPfWStages) + 1u) & 1u, status);
+                    PFC_MARK(PF_PR_WEMPTY);
                     if (!ok) break;
-                    mbar_arrive_expect_tx(&H.wfull[ws], wbytes);
+                    if (valid) {
+                        mbar_arrive_expect_tx(&H.wfull[ws], wbytes);
+                        for (int m = 0; m < nm; ++m)
+                            tma_load_3d(Wring + ws * kPfWStage + m * (4 * 8 * 32 * u.K), wmap[m], 0, u.strip * 8,
+                                        s * 4, &H.wfull[ws]);
+                    } else {
+                        mbar_arrive(&H.wfull[ws]);        // garbage weights; the error bit is set
+                    }
                     issued_w = gs + 1;
-                    for (int m = 0; m < nm; ++m)
-                        for (int i = 0; i < 4; ++i) {
-                            const uint8_t* src = tr[m] == p.dummy
-                                                     ? tr[m]
-                                                     : tr[m] + (int64_t) (s * 4 + i) * slice_bytes + u.strip * 8 * tile_bytes;
-                            bulk_g2s(Wring + ws * kPfWStage + (m * 4 + i) * 8 * tile_bytes, src,
-                                     (uint32_t) (8 * tile_bytes), &H.wfull[ws]);
-                        }
+                    PFC_RESET();
                     ok = mbar_wait(&H.xfree[xs], ((gs / kPfXStages) + 1u) & 1u, status);
+                    PFC_MARK(PF_PR_XFREE);
                     if (!ok) break;
-                    mbar_arrive_expect_tx(&H.xfull[xs], (uint32_t) (nm * kPfXBox));
+                    mbar_arrive_expect_tx(&H.xfull[xs], (uint32_t) (nm * nbox * kPfBoxBytes));
                     for (int m = 0; m < nm; ++m)
-                        tma_load_2d(Xbuf + xs * kPfXStage + m * kPfXBox, xmap[m], s * kPfKStep, u.row0, &H.xfull[xs]);
+                        for (int b = 0; b < nbox; ++b)
+                            tma_load_2d(Xbuf + xs * kPfXStage + m * kPfXBox + b * kPfBoxBytes, xmap[m], s * kPfKStep,
+                                        u.row0 + b * kPfBoxRows, &H.xfull[xs]);
                     issued_x = gs + 1;
                 }
             }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        }
+        if (lane == 0) {
+            PFC_FLUSH(PF_PR_TOTAL, 0);
             // no copy may still be in flight when the CTA retires
             for (uint32_t i = issued_w > kPfWStages ? issued_w - kPfWStages : 0; i < issued_w; ++i)
                 if (!mbar_wait(&H.wfull[i % kPfWStages], (i / kPfWStages) & 1u, status)) break;
@@ -471,14 +609,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         if (lane == 0) {
             uint32_t gs = 0;
             bool ok = true;
+            PFC_DECL
             for (uint32_t n = 0; ok; ++n) {
                 const int d = n % kPfDQ;
+                PFC_RESET();
                 if (!mbar_wait(&H.dfull[d], (n / kPfDQ) & 1u, status)) break;
+                PFC_MARK(PF_MMA_DESC);
                 const PfUnit u = H.desc[d];
                 mbar_arrive(&H.dempty[d]);
                 if (u.mode < 0) break;
+                PFC_COUNT(PF_UNITS);
                 const int a = n & 1;
                 ok = mbar_wait(&H.accfree[a], ((n >> 1) + 1u) & 1u, status);
+                PFC_MARK(PF_MMA_ACCFREE);
                 if (!ok) break;
                 tc_fence_after();
                 const int nm = u.mode == 0 ? 2 : 1;
@@ -486,8 +629,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 const uint32_t acc0 = tmem + (uint32_t) (a * 256);
                 for (int s = 0; s < u.ksteps; ++s, ++gs) {
                     const int as = gs % kPfAStages, xs = gs % kPfXStages;
-                    ok = mbar_wait(&H.xfull[xs], (gs / kPfXStages) & 1u, status) &&
-                         mbar_wait(&H.aready[as], (gs / kPfAStages) & 1u, status);
+                    PFC_RESET();
+                    ok = mbar_wait(&H.xfull[xs], (gs / kPfXStages) & 1u, status);
+                    PFC_MARK(PF_MMA_X);
+                    ok = ok && mbar_wait(&H.aready[as], (gs / kPfAStages) & 1u, status);
+                    PFC_MARK(PF_MMA_A);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(Abuf + as * kPfAStage), x0 = smem_u32(Xbuf + xs * kPfXStage);
@@ -501,28 +647,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 }
                 tc_commit(&H.accfull[a]);
             }
+            PFC_FLUSH(PF_MMA_TOTAL, 0);
         }
     } else if (warp < kPfDecWarps) {
         // ------------------------------------------------------------ decoders
         uint32_t gs = 0;
+        PFC_DECL
         for (uint32_t n = 0;; ++n) {
             const int d = n % kPfDQ;
+            PFC_RESET();
             if (!mbar_wait_lanes(&H.dfull[d], (n / kPfDQ) & 1u, status)) break;
+            PFC_MARK(PF_DEC_DESC);
             const PfUnit u = H.desc[d];
             __syncwarp();
             if (lane == 0) mbar_arrive(&H.dempty[d]);
             if (u.mode < 0) break;
-            if (!pf_decode_dispatch<CB>(H, Abuf, Wring, u, gs, warp, lane, status)) break;
+            if (!pf_decode_dispatch<CB>(H, Abuf, Wring, u, gs, warp, lane, status PFC_FWD)) break;
         }
+        PFC_FLUSH(PF_DEC_TOTAL, lane);
     } else {
         // ------------------------------------------------------------ epilogue
         const int lg = warp & 3;               // TMEM lane group of this warp
         const int ew = warp - kPfEpiWarp0;     // 0..3
         float* SG = Stg;
         float* SU = Stg + kPfChunkRows * 128;
+        PFC_DECL
         for (uint32_t n = 0;; ++n) {
             const int d = n % kPfDQ;
+            PFC_RESET();
             mbar_wait_lanes(&H.dfull[d], (n / kPfDQ) & 1u, status);
+            PFC_MARK(PF_EP_DESC);
             // the four warps take one verdict: a completed phase stays complete
             // until these warps have released the slot
             named_bar(1, kPfEpiWarps * 32);
@@ -532,7 +686,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             if (lane == 0) mbar_arrive(&H.dempty[d]);
             if (u.mode < 0) break;
             const int a = n & 1;
+            PFC_RESET();
             const bool ok = mbar_wait_lanes(&H.accfull[a], (n >> 1) & 1u, status);
+            PFC_MARK(PF_EP_ACC);
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t) (lg * 32) << 16) + (uint32_t) (a * 256);
             const int col = lg * 32 + lane;
@@ -601,6 +757,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 if (ew == 0 && lane == 0) atom_add_release_gpu(p.ctrl + kPfCtrlWords + u.gp, 1u);
             }
         }
+        if (ew == 0) PFC_FLUSH(PF_EP_TOTAL, lane);
     }
 
     tc_fence_before();
@@ -650,6 +807,42 @@ PFN_cuTensorMapEncodeTiled_v12000 pf_encoder() {
     return fn;
 }
 
+// Weight tensor-map templates for (hidden, inter): [gate/up, down][K - 1],
+// dims [16K, n/16, k/16] u16, box [16K, 8, 4] (4 k-slices of 8 tiles), with
+// a placeholder address every unit replaces.  Cached per shape.
+struct PfTemplates {
+    CUtensorMap t[8];
+};
+
+int pf_templates(int64_t H, int64_t I, void* placeholder, PfTemplates* out) {
+    static std::mutex mu;
+    static std::map<std::pair<int64_t, int64_t>, PfTemplates> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({H, I});
+    if (it != cache.end()) {
+        *out = it->second;
+        return EXL3_OK;
+    }
+    auto encode = pf_encoder();
+    EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "exl3_moe_prefill: cuTensorMapEncodeTiled is not available");
+    PfTemplates T{};
+    for (int kind = 0; kind < 2; ++kind)
+        for (int K = 1; K <= kPfKmax; ++K) {
+            const int64_t k = kind == 0 ? H : I, n = kind == 0 ? I : H;
+            const cuuint64_t dims[3] = {(cuuint64_t) (16 * K), (cuuint64_t) (n / 16), (cuuint64_t) (k / 16)};
+            const cuuint64_t strides[2] = {(cuuint64_t) (32 * K), (cuuint64_t) (n / 16) * (cuuint64_t) (32 * K)};
+            const cuuint32_t box[3] = {(cuuint32_t) (16 * K), 8u, 4u};
+            const cuuint32_t estr[3] = {1u, 1u, 1u};
+            const CUresult r = encode(&T.t[kind * 4 + K - 1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, placeholder, dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            EXL3_REQUIRE(r == CUDA_SUCCESS, EXL3_ERR_CUDA, "exl3_moe_prefill: weight tensor map failed (%d)", (int) r);
+        }
+    cache[{H, I}] = T;
+    *out = T;
+    return EXL3_OK;
+}
+
 template <typename... Args>
 cudaError_t pf_launch(void (*kern)(Args...), dim3 grid, dim3 block, int smem, cudaStream_t s, bool pdl,
                       const std::decay_t<Args>&... args) {
@@ -675,7 +868,8 @@ int64_t pf_chunk_tokens(int64_t E) {
 
 struct PfGeom {
     int64_t cap;                  // pair capacity of one chunk = chunk tokens x topk
-    int64_t off_plan, off_xg, off_xu, off_xd, off_dn, total;
+    int64_t unit_cap;             // work units of one chunk, upper bound
+    int64_t off_plan, off_units, off_maps, off_xg, off_xu, off_xd, off_dn, total;
 };
 
 PfGeom pf_geom(int64_t m, int64_t topk, int64_t H, int64_t I, int64_t E) {
@@ -683,9 +877,16 @@ PfGeom pf_geom(int64_t m, int64_t topk, int64_t H, int64_t I, int64_t E) {
     int64_t ct = pf_chunk_tokens(E);
     if (m < ct) ct = m;
     g.cap = ct * topk;
+    // passes: one per expert with rows plus one per 128 rows
+    const int64_t passes = (E < g.cap ? E : g.cap) + g.cap / kPfRows + 1;
+    g.unit_cap = passes * (H / 128 + I / 128);
     int64_t o = kPfCtrlBytes;
     g.off_plan = o;
     o += align_up((4 * (E + 1) + 2 * g.cap + g.cap) * 4, 256);
+    g.off_units = o;
+    o += align_up(g.unit_cap * 16, 256);
+    g.off_maps = o;
+    o += (int64_t) kPfMaxGrid * kPfMapSlots * 2 * 128;
     g.off_xg = o;
     o += align_up(g.cap * H * 2, 256);
     g.off_xu = o;
@@ -714,6 +915,19 @@ int pf_set_attr() {
 }
 
 }  // namespace
+
+#ifdef EXL3_PHASE_CLOCK
+extern "C" int exl3_pf_phase_read(unsigned long long* out, int n, int reset) {
+    EXL3_REQUIRE(out && n >= 1 && n <= PF_N, EXL3_ERR_ARG, "phase clock: bad output");
+    EXL3_CUDA(cudaDeviceSynchronize());
+    EXL3_CUDA(cudaMemcpyFromSymbol(out, g_pf_phase, sizeof(unsigned long long) * n));
+    if (reset) {
+        static const unsigned long long zero[PF_N] = {};
+        EXL3_CUDA(cudaMemcpyToSymbol(g_pf_phase, zero, sizeof(zero)));
+    }
+    return EXL3_OK;
+}
+#endif
 
 extern "C" int64_t exl3_moe_prefill_scratch_bytes(int64_t m, int64_t topk, int64_t hidden, int64_t inter,
                                                   int64_t n_experts) {
@@ -753,6 +967,7 @@ extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_d
                  "exl3_moe_prefill: x must be fp16/bf16, out fp16/bf16/fp32");
     EXL3_REQUIRE(swiglu_limit > 0.f, EXL3_ERR_ARG, "exl3_moe_prefill: swiglu_limit must be > 0");
     EXL3_REQUIRE(aligned16(scratch), EXL3_ERR_ARG, "exl3_moe_prefill: scratch must be 16-byte aligned");
+    EXL3_REQUIRE(aligned16(x), EXL3_ERR_ARG, "exl3_moe_prefill: x must be 16-byte aligned");
     const PfGeom g = pf_geom(m, topk, hidden, inter, n_experts);
     EXL3_REQUIRE(scratch_bytes >= g.total, EXL3_ERR_ARG, "exl3_moe_prefill: scratch too small (%lld < %lld bytes)",
                  (long long) scratch_bytes, (long long) g.total);
@@ -780,7 +995,7 @@ extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_d
         for (int i = 0; i < 3; ++i) {
             const cuuint64_t dims[2] = {(cuuint64_t) widths[i], (cuuint64_t) rows_cap};
             const cuuint64_t strides[1] = {(cuuint64_t) widths[i] * 2};
-            const cuuint32_t box[2] = {(cuuint32_t) kPfKStep, (cuuint32_t) kPfRows};
+            const cuuint32_t box[2] = {(cuuint32_t) kPfKStep, (cuuint32_t) kPfBoxRows};
             const cuuint32_t estr[2] = {1u, 1u};
             const CUresult r = encode(maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bufs[i], dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -808,9 +1023,18 @@ extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_d
     p.plan.pair_tok = pl + 4 * E1;
     p.plan.pair_exp = pl + 4 * E1 + g.cap;
     p.plan.slot_pair = pl + 4 * E1 + 2 * g.cap;
+    p.plan.units = reinterpret_cast<int4*>(sb + g.off_units);
+    p.plan.unit_cap = (int) g.unit_cap;
     p.xd = reinterpret_cast<__half*>(sb + g.off_xd);
     p.dn = reinterpret_cast<float*>(sb + g.off_dn);
-    p.dummy = sb + g.off_xg;
+    p.maps = reinterpret_cast<CUtensorMap*>(sb + g.off_maps);
+    {
+        PfTemplates T{};
+        const int trc = pf_templates(hidden, inter, sb + g.off_xg, &T);
+        if (trc != EXL3_OK) return trc;
+        for (int i = 0; i < 8; ++i) p.tmpl[i] = T.t[i];
+    }
+    const int grid = di.sms < kPfMaxGrid ? di.sms : kPfMaxGrid;
 
     // the status word reports this call
     EXL3_CUDA(cudaMemsetAsync(p.ctrl + 2, 0, sizeof(uint32_t), s));
@@ -826,17 +1050,16 @@ extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_d
         const int W = (T + 31) / 32;
         EXL3_CUDA(pf_launch(pf_plan_kernel, dim3(1), dim3(1024), (int) (n_experts * W * 4), s, false, idc, T,
                             (int) topk, (int) n_experts, (int) hidden, (int) inter, p.ctrl, p.plan));
-        const int64_t items = (int64_t) T * topk * (hidden / 128) * 2;
-        int64_t ib = (items + 7) / 8;
-        if (ib > (int64_t) di.sms * 16) ib = (int64_t) di.sms * 16;
+        int64_t ib = (int64_t) T * topk;
+        if (ib > (int64_t) di.sms * 8) ib = (int64_t) di.sms * 8;
         EXL3_CUDA(pf_launch(pf_input_kernel, dim3((unsigned) ib), dim3(256), 0, s, true, xc, x_dtype, (int) hidden,
-                            (int) g.cap, (const uint32_t*) p.ctrl, (const int*) p.plan.pair_tok,
+                            (const uint32_t*) p.ctrl, (const int*) p.plan.pair_tok,
                             (const int*) p.plan.pair_exp, gate_suh, up_suh, reinterpret_cast<__half*>(sb + g.off_xg),
                             reinterpret_cast<__half*>(sb + g.off_xu)));
         switch (cb) {
-            case 0: EXL3_CUDA(pf_launch(pf_gemm_kernel<0>, dim3(di.sms), dim3(kPfThreads), kPfSmem, s, true, p)); break;
-            case 1: EXL3_CUDA(pf_launch(pf_gemm_kernel<1>, dim3(di.sms), dim3(kPfThreads), kPfSmem, s, true, p)); break;
-            default: EXL3_CUDA(pf_launch(pf_gemm_kernel<2>, dim3(di.sms), dim3(kPfThreads), kPfSmem, s, true, p)); break;
+            case 0: EXL3_CUDA(pf_launch(pf_gemm_kernel<0>, dim3(grid), dim3(kPfThreads), kPfSmem, s, true, p)); break;
+            case 1: EXL3_CUDA(pf_launch(pf_gemm_kernel<1>, dim3(grid), dim3(kPfThreads), kPfSmem, s, true, p)); break;
+            default: EXL3_CUDA(pf_launch(pf_gemm_kernel<2>, dim3(grid), dim3(kPfThreads), kPfSmem, s, true, p)); break;
         }
         int64_t gb = ((int64_t) T * (hidden / 4) + 255) / 256;
         if (gb > (int64_t) di.sms * 8) gb = (int64_t) di.sms * 8;

@@ -98,6 +98,14 @@ __device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t cols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(cols) : "memory");
 }
 
+// Stores four 8x8 b16 matrices held in the MMA fragment layout (lane l:
+// row l/4, elements 2(l%4), 2(l%4)+1 of each) to shared memory; lanes 8j..8j+7
+// give the 16-byte row addresses of matrix j.
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};"
+                 :: "r"(addr), "r"(r0), "r"(r1), "r"(r2), "r"(r3) : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (tensor core, TMA) reads of them.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
