@@ -609,6 +609,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         if (lane == 0) {
             uint32_t gs = 0;
             bool ok = true;
+            const uint64_t adesc0 = sdesc_sw128(smem_u32(Abuf)), xdesc0 = sdesc_sw128(smem_u32(Xbuf));
             PFC_DECL
             for (uint32_t n = 0; ok; ++n) {
                 const int d = n % kPfDQ;
@@ -624,7 +625,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 PFC_MARK(PF_MMA_ACCFREE);
                 if (!ok) break;
                 tc_fence_after();
-                const int nm = u.mode == 0 ? 2 : 1;
                 const uint32_t idesc = idesc_f16(128, (u.rows + 15) & ~15);
                 const uint32_t acc0 = tmem + (uint32_t) (a * 256);
                 for (int s = 0; s < u.ksteps; ++s, ++gs) {
@@ -636,12 +636,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     PFC_MARK(PF_MMA_A);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(Abuf + as * kPfAStage), x0 = smem_u32(Xbuf + xs * kPfXStage);
+                    // descriptors advance in 16-byte units: +2 per 16-element k step
+                    const uint64_t ad = adesc0 + (uint64_t) (as * (kPfAStage >> 4));
+                    const uint64_t xd = xdesc0 + (uint64_t) (xs * (kPfXStage >> 4));
+                    const uint32_t en = s != 0;
+                    if (u.mode == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < kPfKStep / 16; ++kk)
-                        for (int m = 0; m < nm; ++m)
-                            tc_mma(acc0 + m * 128, sdesc_sw128(a0 + m * (128 * 128) + kk * 32),
-                                   sdesc_sw128(x0 + m * kPfXBox + kk * 32), idesc, (s | kk) != 0);
+                        for (int kk = 0; kk < kPfKStep / 16; ++kk) {
+                            tc_mma(acc0, ad + 2 * kk, xd + 2 * kk, idesc, en | kk);
+                            tc_mma(acc0 + 128, ad + (128 * 128 >> 4) + 2 * kk, xd + (kPfXBox >> 4) + 2 * kk, idesc,
+                                   en | kk);
+                        }
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < kPfKStep / 16; ++kk) tc_mma(acc0, ad + 2 * kk, xd + 2 * kk, idesc, en | kk);
+                    }
                     tc_commit(&H.afree[as]);
                     tc_commit(&H.xfree[xs]);
                 }

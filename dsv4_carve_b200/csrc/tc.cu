@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) linear_tc_kernel(const __grid_c
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t id0 = idesc_f16(kTcCols, n0), id1 = idesc_f16(kTcCols, n1 > 0 ? n1 : 16);
+            const uint64_t adesc0 = sdesc_sw128(smem_u32(Abuf)), xdesc0 = sdesc_sw128(smem_u32(Xbuf));
             bool ok = true;
             for (int s = 0; s < nsteps && ok; ++s) {
                 const int as = s % kTcAStages, xs = s % kTcXStages;
@@ -197,14 +198,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) linear_tc_kernel(const __grid_c
                      mbar_wait(&H.aready[as], (s / kTcAStages) & 1u, status);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(Abuf + as * kTcABytes), x0 = smem_u32(Xbuf + xs * kTcXBytes);
+                // descriptors advance in 16-byte units: +2 per 16-element k step
+                const uint64_t ad = adesc0 + (uint64_t) (as * (kTcABytes >> 4));
+                const uint64_t xd = xdesc0 + (uint64_t) (xs * (kTcXBytes >> 4));
+                const uint32_t en = s != 0;
+                if (n1 > 0) {
 #pragma unroll
-                for (int kk = 0; kk < kTcKStep / 16; ++kk) {
-                    const uint32_t acc = (s | kk) != 0;
-                    tc_mma(tmem, sdesc_sw128(a0 + kk * 32), sdesc_sw128(x0 + kk * 32), id0, acc);
-                    if (n1 > 0)
-                        tc_mma(tmem + kTcMaxN, sdesc_sw128(a0 + kk * 32),
-                               sdesc_sw128(x0 + kTcMaxN * 128 + kk * 32), id1, acc);
+                    for (int kk = 0; kk < kTcKStep / 16; ++kk) {
+                        tc_mma(tmem, ad + 2 * kk, xd + 2 * kk, id0, en | kk);
+                        tc_mma(tmem + kTcMaxN, ad + 2 * kk, xd + (kTcMaxN * 128 >> 4) + 2 * kk, id1, en | kk);
+                    }
+                } else {
+#pragma unroll
+                    for (int kk = 0; kk < kTcKStep / 16; ++kk) tc_mma(tmem, ad + 2 * kk, xd + 2 * kk, id0, en | kk);
                 }
                 tc_commit(&H.afree[as]);
                 tc_commit(&H.xfree[xs]);
