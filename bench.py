@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--rows", type=int, default=4, help="dense: activation rows R")
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--precise", action="store_true", help="fp16-rounded weights in the MMA")
+    ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: TP sum inside the MoE kernel over NVLink (fused) or NCCL after it")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
@@ -181,13 +183,22 @@ class MoeWorkload:
         from dsv4_carve_b200 import _lib
 
         self._lib = _lib.load()
+        self.exchange = None
+        if world > 1 and args.allreduce == "fused":
+            from dsv4_carve_b200.tp import MoeTpExchange
+
+            self.exchange = MoeTpExchange(None, dev, max_rows=self.T, hidden=self.H)
         self._argv = []
         for li, L in enumerate(self.layers):
             ids, w = self.routes[li]
-            self._argv.append((self.xs[li].data_ptr(), _lib.DT_F16, self.outs[li].data_ptr(), _lib.DT_F16, self.T,
-                               self.H, self.I, *[t.data_ptr() for t in L.table_list()], self.E, L.ktab.data_ptr(),
-                               self.kmax, self.kmax, synth.CB_MCG, ids.data_ptr(), w.data_ptr(), self.topk,
-                               10.0, self.scratch.data_ptr(), self.scratch.numel(), int(args.precise)))
+            argv = (self.xs[li].data_ptr(), _lib.DT_F16, self.outs[li].data_ptr(), _lib.DT_F16, self.T,
+                    self.H, self.I, *[t.data_ptr() for t in L.table_list()], self.E, L.ktab.data_ptr(),
+                    self.kmax, self.kmax, synth.CB_MCG, ids.data_ptr(), w.data_ptr(), self.topk,
+                    10.0, self.scratch.data_ptr(), self.scratch.numel(), int(args.precise))
+            if self.exchange is not None:
+                argv = argv + (self.exchange.table.data_ptr(), self.exchange.rank, self.exchange.world,
+                               self.exchange.max_rows)
+            self._argv.append(argv)
         # pinned host copies for the end-to-end path
         self.h_x = [x.cpu().pin_memory() for x in self.xs]
         self.h_ids = [r[0].cpu().pin_memory() for r in self.routes]
@@ -200,13 +211,22 @@ class MoeWorkload:
         self.d2h = self.T * self.H * 2
 
     def launch(self, i, stream_handle):
-        rc = self._lib.exl3_moe_decode(*self._argv[i % len(self.layers)], stream_handle)
+        fn = self._lib.exl3_moe_decode_tp if self.exchange is not None else self._lib.exl3_moe_decode
+        rc = fn(*self._argv[i % len(self.layers)], stream_handle)
         if rc:
             raise RuntimeError(self._lib.exl3_last_error().decode())
 
     def allreduce(self, out):
-        if self.world > 1:
+        # the fused path has summed over the ranks inside the kernel
+        if self.world > 1 and self.exchange is None:
             self.torch.distributed.all_reduce(out)
+
+    def close(self):
+        if self.exchange is not None:
+            self.torch.distributed.barrier()
+            self.torch.cuda.synchronize()
+            self.exchange.close()
+            self.exchange = None
 
     def step(self, i, stream_handle):
         self.launch(i, stream_handle)
@@ -222,7 +242,7 @@ class MoeWorkload:
         out = self.outs[li]
         ext.lna2_moe_decode(self.d_x[li], out, *L.table_list(), self.d_ids[li], self.d_w[li], self.kmax, 10.0,
                             self.scratch, intermediate=self.I, k_table=L.ktab, codebook=L.cb,
-                            precise=self.args.precise)
+                            precise=self.args.precise, tp_exchange=self.exchange)
         self.allreduce(out)
         self.h_out[li].copy_(out, non_blocking=True)
 
@@ -240,6 +260,8 @@ class MoeWorkload:
                 "intermediate_per_gpu": 2048 // self.world, "route": a.route, "layers_cycled": a.layers,
                 "unique_experts_per_layer": self.uniq,
                 "parallelism": f"tp{self.world}" if self.world > 1 else "single",
+                "allreduce": ((self.args.allreduce if self.args.allreduce == "nccl" else "fused-nvlink")
+                              if self.world > 1 else None),
                 "l2": "inputs larger than L2 (unique bytes per layer > 126 MB; layers cycled)",
                 "precise": bool(a.precise)}
 
@@ -535,6 +557,8 @@ def main():
     if clocks:
         clocks.stop()
         clock_info = clocks.summary(t_wall0, t_wall1)
+    if hasattr(wl, "close"):
+        wl.close()       # every rank, before any rank leaves the group
 
     if rank != 0:
         if world > 1:

@@ -38,6 +38,14 @@ _SIGS = {
                         + [_I64, _P, _I, _I, _I, _P, _P, _I64, C.c_float, _P, _I64, _I, _P]),
     "exl3_moe_decode_noalloc": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
                                 + [_I64, _P, _I, _I, _I, _P, _P, _I64, C.c_float, _I, _P]),
+    "exl3_tp_buffer_bytes": (_I64, [_I, _I64, _I64]),
+    "exl3_tp_buffer_alloc": (_I, [_I, _I64, _I64, _P]),
+    "exl3_tp_buffer_free": (_I, [_P]),
+    "exl3_tp_ipc_handle": (_I, [_P, _P]),
+    "exl3_tp_ipc_open": (_I, [_P, _P]),
+    "exl3_tp_ipc_close": (_I, [_P]),
+    "exl3_moe_decode_tp": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
+                           + [_I64, _P, _I, _I, _I, _P, _P, _I64, C.c_float, _P, _I64, _I, _P, _I, _I, _I64, _P]),
     "exl3_moe_prefill_scratch_bytes": (_I64, [_I64, _I64, _I64, _I64, _I64]),
     "exl3_moe_prefill_chunk_tokens": (_I64, [_I64]),
     "exl3_moe_prefill": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9

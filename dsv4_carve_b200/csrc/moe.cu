@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -150,6 +151,13 @@ struct MoeParams {
     uint32_t* ag;               // down-input fragments: per pair (I/16) row-slices
     float* partB;               // [pairs][nkb][H] (== downc when nkb == 1)
     float* downc;               // [pairs][H]
+    // Fused tensor-parallel sum (exl3_moe_decode_tp; tp_world == 0: none).
+    // Every rank holds an exchange buffer (tp_buffer_* below); the CTA that
+    // gathers a hidden block pushes its partial rows into slot [rank] of
+    // every rank's buffer, raises its flag there, waits for all ranks' flags
+    // in its own buffer and writes the rank-ordered fp32 sum.
+    const int64_t* tp_bufs;     // [world] device addresses of the ranks' exchange buffers
+    int tp_rank, tp_world, tp_mcap;
 };
 
 struct MoePlan {
@@ -244,6 +252,8 @@ struct alignas(128) MoeHead {
     uint64_t pempty[2];         // partial tile stored by the epilogue warp
     int desc[kMoeDQ][8];        // kind, group, mat, block, chunk, K
     int last_cta;
+    int retire_rank;            // order in which this CTA retired
+    uint32_t tp_epoch;          // this launch's exchange epoch (fused TP sum)
     alignas(128) CUtensorMap tmap;   // the producer's tensor map under construction
 };
 constexpr int kMoeHeadBytes = (int) ((sizeof(MoeHead) + 127) / 128 * 128);
@@ -329,10 +339,98 @@ __device__ void moe_finish_a(const MoeParams& p, const MoePlan& P, int g, int bl
     }
 }
 
+// ------------------------------------------------------------------ fused TP sum
+// Exchange buffer of one rank: [0, 256) header (word 0: epoch counter), then
+// partial rows [2 parities][world][mcap][H] of 8-byte words, each one fp32
+// value in the low half and the epoch that wrote it in the high half, stored
+// and loaded as single 8-byte accesses: a reader that sees the epoch sees the
+// value, so no flags and no fences are needed (the low-latency format NCCL
+// uses for small messages).  Parity = epoch & 1: a rank reaches epoch e + 2
+// only after every rank has pushed e + 1, which each does only after its own
+// epoch-e launch has finished reading, so one parity is never written while
+// it is read.
+constexpr int kTpHeader = 256;
+__host__ __device__ inline int64_t tp_buffer_bytes_for(int world, int64_t mcap, int64_t H) {
+    return kTpHeader + (int64_t) 2 * world * mcap * H * 8;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_v2(uint64_t* p, uint64_t a, uint64_t b) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" :: "l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Row r of this rank's partial of hidden block blk (4 values per lane) into
+// slot [rank] of every rank's exchange buffer.
+__device__ __forceinline__ void tp_push_row(const MoeParams& p, uint32_t epoch, int blk, int lane, int r,
+                                            const float (&v)[4]) {
+    const int W = p.tp_world, par = (int) (epoch & 1u);
+    const uint64_t tag = (uint64_t) epoch << 32;
+    const uint64_t w0 = tag | __float_as_uint(v[0]), w1 = tag | __float_as_uint(v[1]);
+    const uint64_t w2 = tag | __float_as_uint(v[2]), w3 = tag | __float_as_uint(v[3]);
+    for (int j = 0; j < W; ++j) {
+        uint64_t* dst = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.tp_bufs[j]) + kTpHeader) +
+                        (((int64_t) par * W + p.tp_rank) * p.tp_mcap + r) * p.H + blk * kCols + lane * 4;
+        st_relaxed_sys_v2(dst, w0, w1);
+        st_relaxed_sys_v2(dst + 2, w2, w3);
+    }
+}
+
+__device__ __forceinline__ void ld_relaxed_sys_v2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
+}
+
+// Wait (bounded) until word *e carries `epoch`; returns it.
+__device__ __noinline__ uint64_t tp_wait_word(const uint64_t* e, uint32_t epoch, bool& ok) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < kSpinCap; ++i) {
+        __nanosleep(32);
+        const uint64_t v = ld_relaxed_sys(e);
+        if ((uint32_t) (v >> 32) == epoch) return v;
+        if ((i & 63u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    ok = false;
+    return 0;
+}
+
+// Row r of block blk of the output, by one warp (4 values per lane): the sum
+// over ranks, in rank order, of their partials in this rank's buffer.  Two
+// ranks' words are loaded before any is tested, so their latencies overlap;
+// a word that does not carry this launch's epoch yet is waited for (bounded).
+__device__ void tp_finish_row(const MoeParams& p, uint32_t epoch, int blk, int r, int lane, bool& ok) {
+    const int W = p.tp_world, par = (int) (epoch & 1u);
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(reinterpret_cast<const uint8_t*>(p.tp_bufs[p.tp_rank]) +
+                                                            kTpHeader) +
+                          ((int64_t) par * W * p.tp_mcap + r) * p.H + blk * kCols + lane * 4;
+    const int64_t rs = (int64_t) p.tp_mcap * p.H;   // words between ranks' slots
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < W; j += 2) {
+        uint64_t v[2][4];
+        const int nj = j + 1 < W ? 2 : 1;
+        for (int jj = 0; jj < nj; ++jj) {
+            ld_relaxed_sys_v2(src + (j + jj) * rs, v[jj][0], v[jj][1]);
+            ld_relaxed_sys_v2(src + (j + jj) * rs + 2, v[jj][2], v[jj][3]);
+        }
+        for (int jj = 0; jj < nj; ++jj)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint64_t w = v[jj][q];
+                if ((uint32_t) (w >> 32) != epoch) w = ok ? tp_wait_word(src + (j + jj) * rs + q, epoch, ok) : 0;
+                s[q] += __uint_as_float((uint32_t) w);
+            }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
+}
+
 // Phase-B epilogue of (group g, hidden block blk), by one warp: sum the down
 // partials, output transform (lna_moe_ticket.cu:368-378); the last group to
 // finish block blk gathers it for every row in slot order (:409-428).
-__device__ void moe_finish_b(const MoeParams& p, const MoePlan& P, int g, int blk, int lane, uint32_t* cntG) {
+__device__ void moe_finish_b(const MoeParams& p, const MoePlan& P, int g, int blk, int lane, uint32_t* cntG,
+                             uint32_t epoch, uint32_t* status) {
     const int e = P.gexp[g];
     const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
     const __half* dsv = reinterpret_cast<const __half*>(p.tab[8][e]) + blk * kCols;
@@ -371,8 +469,13 @@ __device__ void moe_finish_b(const MoeParams& p, const MoePlan& P, int g, int bl
                 s[0] += wv * d.x; s[1] += wv * d.y; s[2] += wv * d.z; s[3] += wv * d.w;
             }
         }
+        if (p.tp_world > 0) {
+            tp_push_row(p, epoch, blk, lane, r, s);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
+            for (int q = 0; q < 4; ++q)
+                store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
+        }
     }
 }
 
@@ -392,6 +495,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
     uint32_t* cntG = p.ctrl + kOffCntG;
 
     if (tid == 0) {
+        S.tp_epoch = p.tp_world > 0 ? __ldcg(reinterpret_cast<const uint32_t*>(p.tp_bufs[p.tp_rank])) + 1u : 0u;
         for (int s = 0; s < p.ring.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kMoeConsumerWarps); }
         for (int s = 0; s < kMoeDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], kMoeConsumerWarps + 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&S.pfull[s], kMoeConsumerWarps); mbar_init(&S.pempty[s], 1); }
@@ -596,7 +700,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 PHASE_MARK(PH_FIN_A);
             } else {
                 PHASE_COUNT(PH_FINS_B);
-                moe_finish_b(p, P, g, blk, lane, cntG);
+                moe_finish_b(p, P, g, blk, lane, cntG, S.tp_epoch, status);
                 PHASE_MARK(PH_FIN_B);
             }
         }
@@ -682,8 +786,19 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         __threadfence();
         const uint32_t old = atomicAdd(&p.ctrl[1], 1u);
         S.last_cta = old == gridDim.x - 1;
+        S.retire_rank = (int) old;
     }
     __syncthreads();
+    if (p.tp_world > 0 && G > 0) {
+        // TP sum: the k-th CTA to retire (its units are done and no ticket is
+        // left, so its waits hold up nothing) finishes output blocks k,
+        // k + grid, ..., one row per warp at a time.
+        bool ok = true;
+        for (int blk = S.retire_rank; blk < NBH; blk += (int) gridDim.x)
+            for (int r = warp; r < p.m; r += kMoeThreads / 32) tp_finish_row(p, S.tp_epoch, blk, r, lane, ok);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok && lane == 0) set_error(status, ERR_DEP_TIMEOUT);
+    }
     if (S.last_cta) {
         __threadfence();
         for (int i = tid; i < G * 2 * kMoeMaxNka; i += kMoeThreads) readyP[i] = 0u;
@@ -692,6 +807,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             atomicExch(&p.ctrl[0], 0u);
             atomicExch(&p.ctrl[3], 0u);
             atomicExch(&p.ctrl[1], 0u);
+            // the next launch exchanges under the next epoch
+            if (p.tp_world > 0) atomicExch(reinterpret_cast<uint32_t*>(p.tp_bufs[p.tp_rank]), S.tp_epoch);
         }
     }
 }
@@ -907,13 +1024,22 @@ extern "C" int exl3_phase_clock_read(unsigned long long* out, int n, int reset) 
 }
 #endif
 
-extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
-                               int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
-                               const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
-                               const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
-                               const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
-                               int cb, const int32_t* ids, const float* weights, int64_t topk, float swiglu_limit,
-                               void* scratch, int64_t scratch_bytes, int precise, void* stream) {
+namespace exl3 {
+namespace {
+
+struct TpArgs {
+    const int64_t* bufs = nullptr;   // device [world] exchange-buffer addresses
+    int rank = 0, world = 0;
+    int64_t mcap = 0;
+};
+
+int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden, int64_t inter,
+                    const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
+                    const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
+                    const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh, int64_t n_experts,
+                    const int32_t* k_table, int K, int kmax, int cb, const int32_t* ids, const float* weights,
+                    int64_t topk, float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise,
+                    const TpArgs& tp, void* stream) {
     EXL3_REQUIRE(x && out && ids && weights && scratch, EXL3_ERR_ARG, "moe: null pointer argument");
     const int64_t* tabs[9] = {gate_trellis, gate_suh, gate_svh, up_trellis, up_suh,
                               up_svh,       down_trellis, down_suh, down_svh};
@@ -979,6 +1105,10 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     // With a single k-chunk over I a block's partial is its full sum: the
     // epilogue reads it and writes the transformed value in place.
     p.partB = g.nkb > 1 ? reinterpret_cast<float*>(sb + g.off_partB) : p.downc;
+    p.tp_bufs = tp.bufs;
+    p.tp_rank = tp.rank;
+    p.tp_world = tp.world;
+    p.tp_mcap = (int) tp.mcap;
     ring_geom(m, k_table ? kmax : K, precise != 0, &p.ring.wpart, &p.ring.slot_bytes, &p.ring.ns);
 
     const int smem = kMoeHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * (int) m * kCols * 4;
@@ -998,6 +1128,98 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
     }
     EXL3_CUDA(cudaGetLastError());
     return EXL3_OK;
+}
+
+}  // namespace
+}  // namespace exl3
+
+extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
+                               int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
+                               const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
+                               const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
+                               const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
+                               int cb, const int32_t* ids, const float* weights, int64_t topk, float swiglu_limit,
+                               void* scratch, int64_t scratch_bytes, int precise, void* stream) {
+    return exl3::moe_decode_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
+                                 up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K,
+                                 kmax, cb, ids, weights, topk, swiglu_limit, scratch, scratch_bytes, precise,
+                                 exl3::TpArgs{}, stream);
+}
+
+// ------------------------------------------------------------------ fused tensor-parallel sum
+extern "C" int64_t exl3_tp_buffer_bytes(int world, int64_t max_rows, int64_t hidden) {
+    if (world < 1 || world > 32 || max_rows < 1 || max_rows > exl3::kMoeMaxRows || hidden < 128 ||
+        hidden > exl3::kMoeMaxHidden || hidden % 128)
+        return -1;
+    return exl3::tp_buffer_bytes_for(world, max_rows, hidden);
+}
+
+extern "C" int exl3_tp_buffer_alloc(int world, int64_t max_rows, int64_t hidden, void** out) {
+    EXL3_REQUIRE(out, EXL3_ERR_ARG, "tp buffer: null output pointer");
+    const int64_t bytes = exl3_tp_buffer_bytes(world, max_rows, hidden);
+    EXL3_REQUIRE(bytes > 0, EXL3_ERR_ARG, "tp buffer: world 1..32, rows 1..%d, hidden a multiple of 128 <= %d",
+                 exl3::kMoeMaxRows, exl3::kMoeMaxHidden);
+    void* p = nullptr;
+    EXL3_CUDA(cudaMalloc(&p, (size_t) bytes));
+    const cudaError_t e = cudaMemset(p, 0, (size_t) bytes);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        EXL3_CUDA(e);
+    }
+    *out = p;
+    return EXL3_OK;
+}
+
+extern "C" int exl3_tp_buffer_free(void* p) {
+    if (p) EXL3_CUDA(cudaFree(p));
+    return EXL3_OK;
+}
+
+extern "C" int exl3_tp_ipc_handle(void* p, void* handle) {
+    EXL3_REQUIRE(p && handle, EXL3_ERR_ARG, "tp ipc: null pointer");
+    cudaIpcMemHandle_t h;
+    EXL3_CUDA(cudaIpcGetMemHandle(&h, p));
+    memcpy(handle, &h, sizeof(h));
+    return EXL3_OK;
+}
+
+extern "C" int exl3_tp_ipc_open(const void* handle, void** out) {
+    EXL3_REQUIRE(handle && out, EXL3_ERR_ARG, "tp ipc: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    EXL3_CUDA(cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess));
+    return EXL3_OK;
+}
+
+extern "C" int exl3_tp_ipc_close(void* p) {
+    if (p) EXL3_CUDA(cudaIpcCloseMemHandle(p));
+    return EXL3_OK;
+}
+
+extern "C" int exl3_moe_decode_tp(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
+                                  int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
+                                  const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
+                                  const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
+                                  const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
+                                  int cb, const int32_t* ids, const float* weights, int64_t topk,
+                                  float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise,
+                                  const int64_t* tp_bufs, int tp_rank, int tp_world, int64_t tp_max_rows,
+                                  void* stream) {
+    EXL3_REQUIRE(tp_bufs, EXL3_ERR_ARG, "moe tp: null exchange-buffer table");
+    EXL3_REQUIRE(tp_world >= 1 && tp_world <= 32 && tp_rank >= 0 && tp_rank < tp_world, EXL3_ERR_ARG,
+                 "moe tp: rank %d of world %d out of range (world 1..32)", tp_rank, tp_world);
+    EXL3_REQUIRE(m <= tp_max_rows && tp_max_rows <= exl3::kMoeMaxRows, EXL3_ERR_ARG,
+                 "moe tp: m = %lld above the exchange buffers' row capacity %lld", (long long) m,
+                 (long long) tp_max_rows);
+    exl3::TpArgs tp;
+    tp.bufs = tp_bufs;
+    tp.rank = tp_rank;
+    tp.world = tp_world;
+    tp.mcap = tp_max_rows;
+    return exl3::moe_decode_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
+                                 up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K,
+                                 kmax, cb, ids, weights, topk, swiglu_limit, scratch, scratch_bytes, precise, tp,
+                                 stream);
 }
 
 // ------------------------------------------------------------------ allocation-free variant

@@ -221,10 +221,13 @@ def lna2_moe_decode(x: torch.Tensor, out: torch.Tensor,
                     expert_ids: torch.Tensor, routing_weights: torch.Tensor, K: int,
                     swiglu_limit: float, scratch: torch.Tensor, *, intermediate: int = 256,
                     k_table: torch.Tensor | None = None, codebook: int = 1,
-                    precise: bool = False) -> torch.Tensor:
+                    precise: bool = False, tp_exchange=None) -> torch.Tensor:
     """Routed-expert decode of one layer; writes and returns `out`.
 
-    Argument checks follow recipe-lna/lna2/lna_moe_ticket.cu:516-553."""
+    Argument checks follow recipe-lna/lna2/lna_moe_ticket.cu:516-553.  With
+    `tp_exchange` (a dsv4_carve_b200.tp.MoeTpExchange), the tensor-parallel
+    sum of the layer output over the exchange's ranks is done inside the
+    kernel and every rank's `out` holds the full sum."""
     _check(x.is_cuda and x.dtype in (torch.float16, torch.bfloat16),
            "LNA2 input must be CUDA fp16 or bf16")
     _check(x.dim() == 2 and x.size(1) % 128 == 0, "LNA2 input must be [m,hidden] with hidden % 128 == 0")
@@ -264,10 +267,19 @@ def lna2_moe_decode(x: torch.Tensor, out: torch.Tensor,
         kt_ptr, kmax = k_table.data_ptr(), int(K)
         bits = kmax
     with _on_device(x.device):
-        _lib.call("exl3_moe_decode", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
-                  x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
-                  kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
-                  scratch.data_ptr(), scratch.numel(), int(bool(precise)), _stream(x.device))
+        if tp_exchange is None:
+            _lib.call("exl3_moe_decode", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                      x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
+                      kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
+                      scratch.data_ptr(), scratch.numel(), int(bool(precise)), _stream(x.device))
+        else:
+            _check(tp_exchange.table.device == x.device and tp_exchange.hidden == x.size(1)
+                   and x.size(0) <= tp_exchange.max_rows, "LNA2 TP exchange does not match this call")
+            _lib.call("exl3_moe_decode_tp", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                      x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
+                      kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
+                      scratch.data_ptr(), scratch.numel(), int(bool(precise)), tp_exchange.table.data_ptr(),
+                      tp_exchange.rank, tp_exchange.world, tp_exchange.max_rows, _stream(x.device))
     return out
 
 

@@ -157,6 +157,43 @@ int exl3_moe_decode_noalloc(const void* x, int x_dtype, void* out, int out_dtype
                             const int32_t* ids, const float* weights, int64_t topk,
                             float swiglu_limit, int precise, void* stream);
 
+/* ------------------------------------------------------------------ fused TP sum
+ * exl3_moe_decode with the tensor-parallel all-reduce of the layer output
+ * done inside the kernel over NVLink peer memory, replacing the per-layer
+ * NCCL all-reduce the reference runs after lna2_moe_decode
+ * (recipe-lna/vllm_exl3_exl3.py.lna:855-871 shards the experts).  Every
+ * rank holds one exchange buffer (exl3_tp_buffer_alloc, zeroed; its handle
+ * is shared with exl3_tp_ipc_handle / exl3_tp_ipc_open) and passes the
+ * device table `tp_bufs` [world] of all ranks' buffer addresses, its own
+ * included.  The CTA that finishes a 128-column block of the output stores
+ * this rank's partial rows into every rank's buffer, each fp32 value in one
+ * 8-byte word with the launch's epoch beside it; the last CTA to retire waits
+ * (bounded, 2 s) until every rank's values carry the epoch and writes the
+ * fp32 sum over ranks in rank order, then one cast: every rank ends with the
+ * same `out`.  Peer stores and loads only: no multicast, no NVLS.  The epoch
+ * that tells launches apart lives in the buffer, so calls can be captured in
+ * a CUDA graph.  All ranks must make the same sequence of calls with the
+ * same m and routes; a rank that does not arrive sets status bit 0 on the
+ * others after 2 s.  m <= tp_max_rows (the buffers' row capacity).
+ * No counterpart in the reference, which calls NCCL after its kernel. */
+int64_t exl3_tp_buffer_bytes(int world, int64_t max_rows, int64_t hidden);
+int exl3_tp_buffer_alloc(int world, int64_t max_rows, int64_t hidden, void** out);
+int exl3_tp_buffer_free(void* buffer);
+/* cudaIpcMemHandle_t of a buffer (64 bytes) / mapping of a peer's buffer. */
+int exl3_tp_ipc_handle(void* buffer, void* handle64);
+int exl3_tp_ipc_open(const void* handle64, void** out);
+int exl3_tp_ipc_close(void* mapped);
+int exl3_moe_decode_tp(const void* x, int x_dtype, void* out, int out_dtype,
+                       int64_t m, int64_t hidden, int64_t inter,
+                       const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
+                       const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
+                       const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh,
+                       int64_t n_experts, const int32_t* k_table, int K, int kmax, int cb,
+                       const int32_t* ids, const float* weights, int64_t topk,
+                       float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise,
+                       const int64_t* tp_bufs, int tp_rank, int tp_world, int64_t tp_max_rows,
+                       void* stream);
+
 /* ------------------------------------------------------------------ prefill MoE
  * The routed-expert layer of exl3_moe_decode for many rows (prefill chunks)
  * on the tcgen05 tensor cores: same arguments and semantics (gate / up / down

@@ -214,3 +214,29 @@ def test_plugin_dispatch(cuda, oracle):
     assert M.moe_kernel_call_counts()["b200"] == 1
     want, _ = run_oracle(oracle, L0, x, ids, w)
     check(out, want)
+
+
+def test_fused_tp_sum_world_of_one(cuda):
+    """The in-kernel tensor-parallel sum with a world of one (the exchange
+    runs against this rank's own buffer): bitwise the plain output, over
+    several calls (both epoch parities)."""
+    from dsv4_carve_b200.tp import MoeTpExchange
+
+    E, H, I, T, topk = 16, 1024, 256, 4, 4
+    L = to_device(layer(E, H, I, synth.expert_bits(E, 3), 3), cuda)
+    ex = MoeTpExchange.single(cuda, max_rows=8, hidden=H)
+    try:
+        for it in range(5):
+            ids, w = synth.route_uniform(T, E, topk, seed=50 + it)
+            x = synth.activations(T, H, seed=60 + it, device=cuda)
+            ref, _ = run_kernel(L, x, ids, w)
+            got = torch.empty_like(ref)
+            scratch = torch.zeros(ext.lna2_moe_scratch_bytes(T, topk, H, I), dtype=torch.uint8, device=cuda)
+            ext.lna2_moe_decode(x, got, *L.table_list(), ids.to(cuda), w.to(cuda), max(L.kbits), 10.0, scratch,
+                                intermediate=I, k_table=L.ktab, codebook=L.cb, tp_exchange=ex)
+            torch.cuda.synchronize(cuda)
+            assert torch.equal(got, ref)
+            assert ext.lna2_moe_status(scratch) == 0
+    finally:
+        torch.cuda.synchronize(cuda)
+        ex.close()
