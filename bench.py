@@ -54,9 +54,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--tokens", type=int, default=4)
     ap.add_argument("--route", choices=["uniform", "zipf"], default="uniform")
-    ap.add_argument("--config", choices=["moe", "dense"], default="moe",
+    ap.add_argument("--config", choices=["moe", "dense", "prefill"], default="moe",
                     help="moe: config 2/3 routed-MoE layer (the headline); dense: config 1 K6 linears")
     ap.add_argument("--rows", type=int, default=4, help="dense: activation rows R")
+    ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill: tokens per chunk")
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--precise", action="store_true", help="fp16-rounded weights in the MMA")
     ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
@@ -85,6 +86,66 @@ def measured_peak():
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+class NvmlClockSampler:
+    """SM clock, max clock, power and clock-event reasons of this GPU read
+    through NVML every few milliseconds while running (reading only), so
+    that even a timed region of a few tens of milliseconds holds samples."""
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
+
+    def __init__(self, bus_id: str | None, period_s: float = 0.004):
+        import pynvml
+
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.h = None
+        n = pynvml.nvmlDeviceGetCount()
+        for i in range(n):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            pci = pynvml.nvmlDeviceGetPciInfo(h).busId
+            pci = pci.decode() if isinstance(pci, bytes) else pci
+            if bus_id and pci.lower().endswith(str(bus_id).lower()):
+                self.h = h
+        if self.h is None:
+            raise RuntimeError("NVML: no device with this PCI bus id")
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        self.period = period_s
+        self.samples: list = []
+        self.run = False
+        self.t = None
+
+    def start(self):
+        self.run = True
+        self.t = threading.Thread(target=self._loop, daemon=True)
+        self.t.start()
+
+    def _loop(self):
+        nv = self.nv
+        while self.run:
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+                self.samples.append((time.time(), sm, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def stop(self):
+        self.run = False
+        if self.t is not None:
+            self.t.join(timeout=2)
+
+    def summary(self, t0: float, t1: float):
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        use = inside or self.samples
+        if not use:
+            return None
+        reasons = sorted({n for _, _, rs in use for n, b in self.REASONS if rs & b})
+        return {"sm_mhz": statistics.median(sm for _, sm, _ in use), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(use), "in_region": bool(inside), "source": "nvml"}
 
 
 class ClockSampler:
@@ -264,6 +325,99 @@ class MoeWorkload:
                               if self.world > 1 else None),
                 "l2": "inputs larger than L2 (unique bytes per layer > 126 MB; layers cycled)",
                 "precise": bool(a.precise)}
+
+
+class PrefillWorkload:
+    """Config 4b: one routed-MoE layer over a 512-token prefill chunk through
+    the tensor-core path (exl3_moe_prefill): bf16 activations N(0,1), top-8 of
+    256 experts (router N(0,1), softmax over the 8), per-expert K2/K3, MCG,
+    hidden 4096, intermediate 2048 / N per rank.  Two layers are cycled
+    (2 x ~2 GB of packed weights at one GPU, > L2).  N > 1: TP shards of the
+    intermediate dim and one NCCL all-reduce of the [512, 4096] output."""
+
+    launches_per_step = 4
+    kernel_name = "exl3::pf_gemm_kernel"
+    metric = ("prefill MoE layer (config 4b: 512 tokens bf16, top-8 of 256, K2/K3, hidden 4096): "
+              "packed-weight HBM GB/s")
+
+    def __init__(self, args, rank, world, dev):
+        import torch
+
+        from dsv4_carve_b200 import _lib, synth
+        from dsv4_carve_b200 import vllm_exl3_c as ext
+
+        self.torch, self.ext, self.args, self.world, self.dev = torch, ext, args, world, dev
+        self.E, self.H, self.I_full, self.T, self.topk = args.experts, 4096, 2048, args.prefill_tokens, 8
+        self.I = self.I_full // world
+        self.rows = self.T
+        self.lib = _lib.load()
+        self.layers, self.routes, self.xs, self.outs, self.ubytes, self.uniq, self._argv = [], [], [], [], [], [], []
+        nl = max(1, min(2, args.layers))
+        self.scratch = torch.empty(ext.lna2_moe_prefill_scratch_bytes(self.T, self.topk, self.H, self.I, self.E),
+                                   dtype=torch.uint8, device=dev)
+        for li in range(nl):
+            seed = 3000 + li
+            kbits = synth.expert_bits(self.E, seed)
+            L = synth.make_moe_layer(self.E, self.H, self.I_full, kbits, seed, device=dev, cb=synth.CB_MCG,
+                                     rank=rank, world=world)
+            ids, w = synth.route_uniform(self.T, self.E, self.topk, seed=seed + 7, device=dev)
+            x = synth.activations(self.T, self.H, seed=seed + 11, device=dev, dtype=torch.bfloat16)
+            out = torch.empty((self.T, self.H), dtype=torch.bfloat16, device=dev)
+            self.layers.append(L)
+            self.routes.append((ids, w))
+            self.xs.append(x)
+            self.outs.append(out)
+            self.ubytes.append(L.unique_bytes(ids) + self.T * self.H * 2 * 2)
+            self.uniq.append(int(torch.unique(ids).numel()))
+            self._argv.append((x.data_ptr(), _lib.DT_BF16, out.data_ptr(), _lib.DT_BF16, self.T, self.H, self.I,
+                               *[t.data_ptr() for t in L.table_list()], self.E, L.ktab.data_ptr(), 3, 3,
+                               synth.CB_MCG, ids.data_ptr(), w.data_ptr(), self.topk, 10.0,
+                               self.scratch.data_ptr(), self.scratch.numel()))
+        self.h_x = [x.cpu().pin_memory() for x in self.xs]
+        self.h_ids = [r[0].cpu().pin_memory() for r in self.routes]
+        self.h_w = [r[1].cpu().pin_memory() for r in self.routes]
+        self.h_out = [torch.empty((self.T, self.H), dtype=torch.bfloat16).pin_memory() for _ in self.layers]
+        self.d_ids = [torch.empty_like(r[0]) for r in self.routes]
+        self.d_w = [torch.empty_like(r[1]) for r in self.routes]
+        self.h2d = self.T * self.H * 2 + self.T * self.topk * 8
+        self.d2h = self.T * self.H * 2
+
+    def launch(self, i, stream_handle):
+        rc = self.lib.exl3_moe_prefill(*self._argv[i % len(self.layers)], stream_handle)
+        if rc:
+            raise RuntimeError(self.lib.exl3_last_error().decode())
+
+    def allreduce(self, out):
+        if self.world > 1:
+            self.torch.distributed.all_reduce(out)
+
+    def step(self, i, stream_handle):
+        self.launch(i, stream_handle)
+        self.allreduce(self.outs[i % len(self.layers)])
+
+    def e2e_step(self, i):
+        li = i % len(self.layers)
+        L = self.layers[li]
+        x = self.xs[li]
+        x.copy_(self.h_x[li], non_blocking=True)
+        self.d_ids[li].copy_(self.h_ids[li], non_blocking=True)
+        self.d_w[li].copy_(self.h_w[li], non_blocking=True)
+        out = self.outs[li]
+        self.ext.lna2_moe_prefill(x, out, *L.table_list(), self.d_ids[li], self.d_w[li], 3, 10.0, self.scratch,
+                                  intermediate=self.I, k_table=L.ktab, codebook=L.cb)
+        self.allreduce(out)
+        self.h_out[li].copy_(out, non_blocking=True)
+
+    def bytes_per_step(self, i):
+        return self.ubytes[i % len(self.layers)]
+
+    def describe(self):
+        return {"workload": "config4b_prefill_moe_layer", "tokens": self.T, "topk": 8, "experts": self.E,
+                "hidden": 4096, "intermediate": 2048, "intermediate_per_gpu": self.I, "route": "uniform",
+                "activations": "bf16", "layers_cycled": len(self.layers), "unique_experts_per_layer": self.uniq,
+                "parallelism": f"tp{self.world}" if self.world > 1 else "single",
+                "l2": "inputs larger than L2 (packed weights per layer > 126 MB; layers cycled)",
+                "path": "tcgen05 dequant-then-MMA", "precise": True}
 
 
 class DenseWorkload:
@@ -483,7 +637,7 @@ def main():
         if world > 1:
             torch.distributed.barrier(device_ids=[local])
 
-    wl = (DenseWorkload if args.config == "dense" else MoeWorkload)(args, rank, world, dev)
+    wl = {"dense": DenseWorkload, "prefill": PrefillWorkload}.get(args.config, MoeWorkload)(args, rank, world, dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     for i in range(args.warmup):
@@ -496,7 +650,12 @@ def main():
         bus = f"{int(pr.pci_bus_id):02x}:{int(pr.pci_device_id):02x}.0"
     except Exception:
         bus = None
-    clocks = ClockSampler(bus) if (rank == 0 and not args.no_clocks) else None
+    clocks = None
+    if rank == 0 and not args.no_clocks:
+        try:
+            clocks = NvmlClockSampler(bus)
+        except Exception:
+            clocks = ClockSampler(bus)
     if clocks:
         clocks.start()
         time.sleep(0.6)
@@ -551,7 +710,9 @@ def main():
             torch.distributed.all_reduce(ms2, op=torch.distributed.ReduceOp.MAX)
         e2e = {"value": all_bytes / (float(ms2.item()) / 1e3) / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
-               "ms_per_step": float(ms2.item()) / K, "api": "vllm_exl3_c.lna2_moe_decode"}
+               "ms_per_step": float(ms2.item()) / K,
+               "api": {"dense": "vllm_exl3_c.linear_forward", "prefill": "vllm_exl3_c.lna2_moe_prefill"}.get(
+                   args.config, "vllm_exl3_c.lna2_moe_decode")}
 
     clock_info = None
     if clocks:
@@ -577,7 +738,7 @@ def main():
             traffic = tr["dram_bytes_per_launch"] / tr["algorithmic_bytes_per_launch"] * (my_bytes / K)
         except Exception:
             traffic = None
-    rows = args.rows if args.config == "dense" else args.tokens
+    rows = args.rows if args.config == "dense" else getattr(wl, "rows", args.tokens)
     line = {
         "metric": wl.metric or METRIC, "value": all_bytes / (ms_max / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
         "steps": K, "warmup": args.warmup, "ms_per_step": ms_max / K, "us_per_layer": ms_max / K * 1e3,
