@@ -58,6 +58,8 @@ def parse():
                     help="moe: config 2/3 routed-MoE layer (the headline); dense: config 1 K6 linears")
     ap.add_argument("--rows", type=int, default=4, help="dense: activation rows R")
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill: tokens per chunk")
+    ap.add_argument("--emulate-tp", type=int, default=1,
+                    help="one GPU: run rank 0's shard of a TP-N layer (intermediate / N), no collective")
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--precise", action="store_true", help="fp16-rounded weights in the MMA")
     ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
@@ -217,13 +219,14 @@ class MoeWorkload:
         self.torch, self.ext, self.synth = torch, ext, synth
         self.args, self.rank, self.world, self.dev = args, rank, world, dev
         self.E, self.H, self.I_full, self.T, self.topk = args.experts, 4096, 2048, args.tokens, 8
-        self.I = self.I_full // world
+        self.shards = world if world > 1 else max(1, args.emulate_tp)
+        self.I = self.I_full // self.shards
         self.layers, self.routes, self.xs, self.ubytes, self.uniq = [], [], [], [], []
         for li in range(args.layers):
             seed = 1000 + li
             kbits = synth.expert_bits(self.E, seed)
             L = synth.make_moe_layer(self.E, self.H, self.I_full, kbits, seed, device=dev, cb=synth.CB_MCG,
-                                     rank=rank, world=world)
+                                     rank=rank, world=self.shards)
             if args.route == "zipf":
                 ids, w = synth.route_zipf(self.T, self.E, self.topk, seed=seed + 7, device=dev)
             else:
@@ -245,10 +248,25 @@ class MoeWorkload:
 
         self._lib = _lib.load()
         self.exchange = None
+        self.allreduce_note = None
         if world > 1 and args.allreduce == "fused":
             from dsv4_carve_b200.tp import MoeTpExchange
 
-            self.exchange = MoeTpExchange(None, dev, max_rows=self.T, hidden=self.H)
+            # every rank must agree on the path: the setup outcome is all-reduced
+            try:
+                ex = MoeTpExchange(None, dev, max_rows=self.T, hidden=self.H)
+                ok = torch.ones(1, device=dev)
+            except Exception as exc:      # no peer access: NCCL after the kernel instead
+                ex, ok = None, torch.zeros(1, device=dev)
+                self.allreduce_note = f"fused exchange setup failed ({exc!r}); NCCL used"
+            torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+            if ok.item() == 1:
+                self.exchange = ex
+            else:
+                if ex is not None:
+                    torch.distributed.barrier()
+                    ex.close()
+                self.allreduce_note = self.allreduce_note or "fused exchange setup failed on a peer rank; NCCL used"
         self._argv = []
         for li, L in enumerate(self.layers):
             ids, w = self.routes[li]
@@ -318,11 +336,14 @@ class MoeWorkload:
         a = self.args
         return {"workload": "config2_moe_decode_layer" if a.route == "uniform" else "config3_moe_decode_layer_zipf",
                 "tokens": a.tokens, "topk": 8, "experts": a.experts, "hidden": 4096, "intermediate": 2048,
-                "intermediate_per_gpu": 2048 // self.world, "route": a.route, "layers_cycled": a.layers,
+                "intermediate_per_gpu": self.I, "route": a.route, "layers_cycled": a.layers,
                 "unique_experts_per_layer": self.uniq,
-                "parallelism": f"tp{self.world}" if self.world > 1 else "single",
-                "allreduce": ((self.args.allreduce if self.args.allreduce == "nccl" else "fused-nvlink")
+                "parallelism": (f"tp{self.world}" if self.world > 1 else
+                                f"rank 0 shard of tp{self.shards} on one GPU (no collective)" if self.shards > 1
+                                else "single"),
+                "allreduce": (("nccl" if self.args.allreduce == "nccl" or self.allreduce_note else "fused-nvlink")
                               if self.world > 1 else None),
+                "allreduce_note": self.allreduce_note,
                 "l2": "inputs larger than L2 (unique bytes per layer > 126 MB; layers cycled)",
                 "precise": bool(a.precise)}
 
@@ -348,7 +369,8 @@ class PrefillWorkload:
 
         self.torch, self.ext, self.args, self.world, self.dev = torch, ext, args, world, dev
         self.E, self.H, self.I_full, self.T, self.topk = args.experts, 4096, 2048, args.prefill_tokens, 8
-        self.I = self.I_full // world
+        self.shards = world if world > 1 else max(1, args.emulate_tp)
+        self.I = self.I_full // self.shards
         self.rows = self.T
         self.lib = _lib.load()
         self.layers, self.routes, self.xs, self.outs, self.ubytes, self.uniq, self._argv = [], [], [], [], [], [], []
@@ -359,7 +381,7 @@ class PrefillWorkload:
             seed = 3000 + li
             kbits = synth.expert_bits(self.E, seed)
             L = synth.make_moe_layer(self.E, self.H, self.I_full, kbits, seed, device=dev, cb=synth.CB_MCG,
-                                     rank=rank, world=world)
+                                     rank=rank, world=self.shards)
             ids, w = synth.route_uniform(self.T, self.E, self.topk, seed=seed + 7, device=dev)
             x = synth.activations(self.T, self.H, seed=seed + 11, device=dev, dtype=torch.bfloat16)
             out = torch.empty((self.T, self.H), dtype=torch.bfloat16, device=dev)
@@ -415,7 +437,9 @@ class PrefillWorkload:
         return {"workload": "config4b_prefill_moe_layer", "tokens": self.T, "topk": 8, "experts": self.E,
                 "hidden": 4096, "intermediate": 2048, "intermediate_per_gpu": self.I, "route": "uniform",
                 "activations": "bf16", "layers_cycled": len(self.layers), "unique_experts_per_layer": self.uniq,
-                "parallelism": f"tp{self.world}" if self.world > 1 else "single",
+                "parallelism": (f"tp{self.world}" if self.world > 1 else
+                                f"rank 0 shard of tp{self.shards} on one GPU (no collective)" if self.shards > 1
+                                else "single"),
                 "l2": "inputs larger than L2 (packed weights per layer > 126 MB; layers cycled)",
                 "path": "tcgen05 dequant-then-MMA", "precise": True}
 

@@ -56,12 +56,13 @@
 namespace exl3 {
 
 constexpr int kPfDecWarps = 16;
-constexpr int kPfProducerWarp = 16;
+constexpr int kPfProducerWarp = 16;             // tickets, weight tensor maps, weight stages
 constexpr int kPfMmaWarp = 17;
 constexpr int kPfEpiWarp0 = 18;                 // warps 18..21: TMEM lane groups 2, 3, 0, 1
 constexpr int kPfEpiWarps = 4;
-constexpr int kPfThreads = (kPfEpiWarp0 + kPfEpiWarps) * 32;
-constexpr int kPfRows = 128;                    // rows per pass (MMA N <= 128)
+constexpr int kPfXWarp = 22;                    // activation stages (and the down units' dependency waits)
+constexpr int kPfThreads = (kPfXWarp + 1) * 32;
+constexpr int kPfRows = 64;                     // rows per pass (MMA N <= 64)
 constexpr int kPfKStep = 64;                    // k per step (4 k-slices)
 constexpr int kPfKmax = 4;                      // largest bit width
 constexpr int kPfBoxRows = 16;                 // rows per activation TMA box
@@ -70,9 +71,10 @@ constexpr int kPfXBox = kPfRows * 128;          // one matrix's activation tile 
 constexpr int kPfXStage = 2 * kPfXBox;          // gate + up tiles
 constexpr int kPfXStages = 3;
 constexpr int kPfAStage = 2 * 128 * 128;        // gate + up decoded tiles [128 cols][64 k] fp16
-constexpr int kPfAStages = 2;
+constexpr int kPfAStages = 3;
+static_assert(kPfAStages == 3 && kPfXStages == 3, "one commit frees a step's decoded weights and activations together");
 constexpr int kPfWStage = 2 * 4 * 8 * 32 * kPfKmax;   // 2 matrices x 4 k-slices x 8 tiles at K = 4
-constexpr int kPfWStages = 4;
+constexpr int kPfWStages = 6;
 constexpr int kPfChunkRows = 32;                // epilogue staging rows
 constexpr int kPfStageBytes = 2 * kPfChunkRows * 128 * 4;
 constexpr int kPfDQ = 4;                        // unit descriptor queue depth
@@ -83,7 +85,8 @@ constexpr int kPfMaxTopk = 16;
 constexpr int kPfCtrlWords = 16;                // [0] ticket [2] status [4] gate/up units [5] down units [6] pairs
 constexpr int kPfCtrlBytes = 65536;             // control words + per-pass counters
 constexpr int kPfMaxPasses = kPfCtrlBytes / 4 - kPfCtrlWords;
-constexpr int kPfMapSlots = 6;                  // weight tensor maps per matrix per CTA, used in turn by units
+constexpr int kPfMapSlots = 8;                  // weight tensor maps per matrix per CTA, used in turn by units
+static_assert(kPfMapSlots > kPfWStages, "a map slot is reused only after its copies have landed");
 constexpr int kPfMaxGrid = 256;                 // CTAs the map slots are sized for
 constexpr int kPfHeadBytes = 1024;
 
@@ -101,8 +104,9 @@ struct PfUnit {
 struct PfHead {
     CUtensorMap tmap[2];                        // staging of this unit's weight maps (128-byte aligned)
     uint64_t wfull[kPfWStages], wempty[kPfWStages];
-    uint64_t aready[kPfAStages], afree[kPfAStages];
-    uint64_t xfull[kPfXStages], xfree[kPfXStages];
+    uint64_t aready[kPfAStages];
+    uint64_t xfull[kPfXStages];
+    uint64_t sfree[kPfAStages];                 // step buffers (decoded weights + activations) consumed by the MMAs
     uint64_t accfull[2], accfree[2];
     uint64_t dfull[kPfDQ], dempty[kPfDQ];
     PfUnit desc[kPfDQ];
@@ -147,7 +151,7 @@ enum {
     PF_DEC_DESC, PF_DEC_W, PF_DEC_AFREE, PF_DEC_TOTAL,
     PF_MMA_DESC, PF_MMA_ACCFREE, PF_MMA_X, PF_MMA_A, PF_MMA_TOTAL,
     PF_PR_TICKET, PF_PR_DEMPTY, PF_PR_DEP, PF_PR_WEMPTY, PF_PR_XFREE, PF_PR_TOTAL,
-    PF_EP_DESC, PF_EP_ACC, PF_EP_TOTAL, PF_UNITS, PF_N
+    PF_EP_DESC, PF_EP_ACC, PF_EP_TOTAL, PF_UNITS, PF_XP_TOTAL, PF_N
 };
 __device__ unsigned long long g_pf_phase[PF_N];
 struct PfClock {
@@ -413,7 +417,7 @@ __device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, i
         PFC_RESET();
         if (!mbar_wait_lanes(&H.wfull[ws], (gs / kPfWStages) & 1u, status)) return false;
         PFC_MARK(PF_DEC_W);
-        if (!mbar_wait_lanes(&H.afree[as], ((gs / kPfAStages) + 1u) & 1u, status)) return false;
+        if (!mbar_wait_lanes(&H.sfree[as], ((gs / kPfAStages) + 1u) & 1u, status)) return false;
         PFC_MARK(PF_DEC_AFREE);
         const uint32_t* wst = reinterpret_cast<const uint32_t*>(Wring + ws * kPfWStage);
         const uint32_t a = abase + (uint32_t) (as * kPfAStage);
@@ -486,12 +490,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
 
     if (tid == 0) {
         for (int s = 0; s < kPfWStages; ++s) { mbar_init(&H.wfull[s], 1); mbar_init(&H.wempty[s], kPfDecWarps); }
-        for (int s = 0; s < kPfAStages; ++s) { mbar_init(&H.aready[s], kPfDecWarps); mbar_init(&H.afree[s], 1); }
-        for (int s = 0; s < kPfXStages; ++s) { mbar_init(&H.xfull[s], 1); mbar_init(&H.xfree[s], 1); }
+        for (int s = 0; s < kPfAStages; ++s) {
+            mbar_init(&H.aready[s], kPfDecWarps);
+            mbar_init(&H.xfull[s], 1);
+            mbar_init(&H.sfree[s], 1);
+        }
         for (int s = 0; s < 2; ++s) { mbar_init(&H.accfull[s], 1); mbar_init(&H.accfree[s], kPfEpiWarps); }
         for (int s = 0; s < kPfDQ; ++s) {
             mbar_init(&H.dfull[s], 1);
-            mbar_init(&H.dempty[s], kPfDecWarps + 1 + kPfEpiWarps);
+            mbar_init(&H.dempty[s], kPfDecWarps + 1 + kPfEpiWarps + 1);
         }
         fence_barrier_init();
     }
@@ -509,7 +516,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         // is reused kPfMapSlots units later, after more weight stages than
         // the ring holds have been issued, so no copy still reads it.
         pdl_wait();
-        uint32_t gs = 0, issued_w = 0, issued_x = 0;
+        uint32_t gs = 0, issued_w = 0;
         bool ok = true;
         const int ngu = (int) __ldcg(p.ctrl + 4), ndn = (int) __ldcg(p.ctrl + 5);
         // the next ticket is claimed one unit ahead, so its latency overlaps
@@ -558,17 +565,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             }
             if (!valid && lane == 0) set_error(status, ERR_MISALIGNED);
             if (lane == 0) {
-                if (u.mode == 1) {
-                    // the down input of this pass: every 128-column strip of I written
-                    ok = wait_counter(p.ctrl + kPfCtrlWords + u.gp, (uint32_t) (p.I / 128), status);
-                    fence_proxy_async_global();
-                }
-                PFC_MARK(PF_PR_DEP);
+                // weights do not depend on earlier units: down units' weights
+                // stream while their input is still being written
                 const uint32_t wbytes = (uint32_t) (nm * 4 * 8 * 32 * u.K);
-                const CUtensorMap* xmap[2] = {u.mode == 0 ? &p.xg_map : &p.xd_map, &p.xu_map};
-                const int nbox = (u.rows + kPfBoxRows - 1) / kPfBoxRows;
                 for (int s = 0; s < u.ksteps && ok; ++s, ++gs) {
-                    const int ws = gs % kPfWStages, xs = gs % kPfXStages;
+                    const int ws = gs % kPfWStages;
                     PFC_RESET();
                     ok = mbar_wait(&H.wempty[ws], ((gs / kPfWStages) + 1u) & 1u, status);
                     PFC_MARK(PF_PR_WEMPTY);
@@ -582,8 +583,45 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                         mbar_arrive(&H.wfull[ws]);        // garbage weights; the error bit is set
                     }
                     issued_w = gs + 1;
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        }
+        if (lane == 0) {
+            PFC_FLUSH(PF_PR_TOTAL, 0);
+            // no copy may still be in flight when the CTA retires
+            for (uint32_t i = issued_w > kPfWStages ? issued_w - kPfWStages : 0; i < issued_w; ++i)
+                if (!mbar_wait(&H.wfull[i % kPfWStages], (i / kPfWStages) & 1u, status)) break;
+        }
+    } else if (warp == kPfXWarp) {
+        // ------------------------------------------------------------ activation producer
+        // Follows the unit descriptors; a down unit first waits (bounded) until
+        // every 128-column strip of its pass's down input is written.
+        pdl_wait();
+        if (lane == 0) {
+            uint32_t gs = 0, issued_x = 0;
+            bool ok = true;
+            PFC_DECL
+            for (uint32_t n = 0; ok; ++n) {
+                const int d = n % kPfDQ;
+                if (!mbar_wait(&H.dfull[d], (n / kPfDQ) & 1u, status)) break;
+                const PfUnit u = H.desc[d];
+                mbar_arrive(&H.dempty[d]);
+                if (u.mode < 0) break;
+                PFC_RESET();
+                if (u.mode == 1) {
+                    ok = wait_counter(p.ctrl + kPfCtrlWords + u.gp, (uint32_t) (p.I / 128), status);
+                    fence_proxy_async_global();
+                    if (!ok) break;
+                }
+                PFC_MARK(PF_PR_DEP);
+                const int nm = u.mode == 0 ? 2 : 1;
+                const CUtensorMap* xmap[2] = {u.mode == 0 ? &p.xg_map : &p.xd_map, &p.xu_map};
+                const int nbox = (u.rows + kPfBoxRows - 1) / kPfBoxRows;
+                for (int s = 0; s < u.ksteps && ok; ++s, ++gs) {
+                    const int xs = gs % kPfXStages;
                     PFC_RESET();
-                    ok = mbar_wait(&H.xfree[xs], ((gs / kPfXStages) + 1u) & 1u, status);
+                    ok = mbar_wait(&H.sfree[xs], ((gs / kPfXStages) + 1u) & 1u, status);
                     PFC_MARK(PF_PR_XFREE);
                     if (!ok) break;
                     mbar_arrive_expect_tx(&H.xfull[xs], (uint32_t) (nm * nbox * kPfBoxBytes));
@@ -594,13 +632,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     issued_x = gs + 1;
                 }
             }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        }
-        if (lane == 0) {
-            PFC_FLUSH(PF_PR_TOTAL, 0);
-            // no copy may still be in flight when the CTA retires
-            for (uint32_t i = issued_w > kPfWStages ? issued_w - kPfWStages : 0; i < issued_w; ++i)
-                if (!mbar_wait(&H.wfull[i % kPfWStages], (i / kPfWStages) & 1u, status)) break;
+            PFC_FLUSH(PF_XP_TOTAL, 0);
             for (uint32_t i = issued_x > kPfXStages ? issued_x - kPfXStages : 0; i < issued_x; ++i)
                 if (!mbar_wait(&H.xfull[i % kPfXStages], (i / kPfXStages) & 1u, status)) break;
         }
@@ -651,8 +683,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
 #pragma unroll
                         for (int kk = 0; kk < kPfKStep / 16; ++kk) tc_mma(acc0, ad + 2 * kk, xd + 2 * kk, idesc, en | kk);
                     }
-                    tc_commit(&H.afree[as]);
-                    tc_commit(&H.xfree[xs]);
+                    tc_commit(&H.sfree[as]);
                 }
                 tc_commit(&H.accfull[a]);
             }
