@@ -31,9 +31,12 @@ namespace exl3 {
 enum Codebook : int { CB_3INST = 0, CB_MCG = 1, CB_MUL1 = 2 };
 
 // Windows per 64-bit group: every group's 16 + (G-1)K stream bits fit in two
-// consecutive uint32 words for any lane (checked for K = 1..8).
+// consecutive uint32 words for any lane (checked for K = 1..8).  Groups are
+// kept short enough that most windows sit at most 16 bits above the group's
+// last one (K <= 5: all of them), which the extraction of tile_windows_f
+// turns into one shift and one byte permute.
 template <int K> struct TileFmt {
-    static constexpr int G = (K <= 4) ? 8 : (K == 7 ? 2 : 4);
+    static constexpr int G = (K <= 2) ? 8 : (K == 7 ? 2 : 4);
     static constexpr int NG = 8 / G;
     static constexpr int WORDS = 8 * K;         // uint32 words per tile
     static constexpr int BYTES = 32 * K;        // bytes per tile
@@ -126,6 +129,54 @@ __device__ __forceinline__ void tile_windows_w(const uint32_t (&whi_)[TileFmt<K>
     }
 }
 
+// Powers of two 2^1 .. 2^15 held in kernel parameters.  A left shift written
+// as a multiply by one of them stays an integer multiply-add (the FMA pipe),
+// because the compiler cannot see the value; the same shift by a literal would
+// be issued to the 16-lane integer ALU pipe, which the decode already fills
+// with its byte permutes and codebook LOP3s.
+struct ShiftTable {
+    uint32_t mul[16];           // mul[i] = 1u << i
+};
+
+inline void shift_table_init(ShiftTable& t) {
+    for (int i = 0; i < 16; ++i) t.mul[i] = 1u << i;
+}
+
+// Window `OFF` bits above the group's last window, zero-extended: byte
+// permutes for byte-aligned offsets; otherwise the window is moved to the top
+// half by an IMAD left shift and taken by a byte permute.  Offsets above 16
+// (K = 6 and 8 only) fall back to the funnel shift of window_at.
+template <int OFF>
+__device__ __forceinline__ uint32_t window_f(uint32_t lo32, uint32_t hi32, const ShiftTable& st) {
+    if constexpr (OFF == 0) return lo32 & 0xffffu;
+    else if constexpr (OFF == 8) return __byte_perm(lo32, 0u, 0x4421);
+    else if constexpr (OFF == 16) return __byte_perm(lo32, 0u, 0x4432);
+    else if constexpr (OFF < 16) return __byte_perm(lo32 * st.mul[16 - OFF], 0u, 0x4432);
+    else return window_at<OFF>(lo32, hi32);
+}
+
+// tile_windows_w with the extraction of window_f (the GEMV engine's decoder).
+template <int K>
+__device__ __forceinline__ void tile_windows_f(const uint32_t (&whi_)[TileFmt<K>::NG],
+                                               const uint32_t (&wlo_)[TileFmt<K>::NG], const LaneGeom<K>& g,
+                                               const ShiftTable& st, uint32_t (&w)[8]) {
+    using F = TileFmt<K>;
+    constexpr int G = F::G;
+#pragma unroll
+    for (int h = 0; h < F::NG; ++h) {
+        const uint32_t lo32 = __funnelshift_r(wlo_[h], whi_[h], g.sh[h]);
+        const uint32_t hi32 = ((G - 1) * K > 16) ? (whi_[h] >> g.sh[h]) : 0u;
+        w[h * G + 0] = window_f<(G - 1) * K>(lo32, hi32, st);
+        if constexpr (G > 1) w[h * G + 1] = window_f<(G - 2) * K>(lo32, hi32, st);
+        if constexpr (G > 2) w[h * G + 2] = window_f<(G > 2 ? G - 3 : 0) * K>(lo32, hi32, st);
+        if constexpr (G > 3) w[h * G + 3] = window_f<(G > 3 ? G - 4 : 0) * K>(lo32, hi32, st);
+        if constexpr (G > 4) w[h * G + 4] = window_f<(G > 4 ? G - 5 : 0) * K>(lo32, hi32, st);
+        if constexpr (G > 5) w[h * G + 5] = window_f<(G > 5 ? G - 6 : 0) * K>(lo32, hi32, st);
+        if constexpr (G > 6) w[h * G + 6] = window_f<(G > 6 ? G - 7 : 0) * K>(lo32, hi32, st);
+        if constexpr (G > 7) w[h * G + 7] = window_f<(G > 7 ? G - 8 : 0) * K>(lo32, hi32, st);
+    }
+}
+
 // 16-bit windows of this lane's 8 weights, j = 0..7, reading the tile at tw.
 template <int K>
 __device__ __forceinline__ void tile_windows(const uint32_t* tw, const LaneGeom<K>& g, uint32_t (&w)[8]) {
@@ -183,6 +234,14 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
 __device__ __forceinline__ void mma_tile(float (&d)[4], const uint32_t (&x)[8], const uint4& bf) {
     mma_16816(d, x[0], x[4], x[2], x[6], bf.x, bf.y);
     mma_16816(d, x[1], x[5], x[3], x[7], bf.z, bf.w);
+}
+
+// mma_tile with the even and odd k rows summed into separate accumulators, so
+// the two MMAs of a tile do not wait on each other; the caller adds d1 to d0
+// at the end of its k range.
+__device__ __forceinline__ void mma_tile2(float (&d0)[4], float (&d1)[4], const uint32_t (&x)[8], const uint4& bf) {
+    mma_16816(d0, x[0], x[4], x[2], x[6], bf.x, bf.y);
+    mma_16816(d1, x[1], x[5], x[3], x[7], bf.z, bf.w);
 }
 
 // PRECISE variant: the weights the reference actually uses, RN(lo + hi) in

@@ -601,6 +601,7 @@ extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, 
     EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "exl3_linear: cuTensorMapEncodeTiled is not available");
 
     LinearParams p{};
+    shift_table_init(p.ring.st);
     {
         const cuuint64_t dims[3] = {(cuuint64_t) (16 * K), (cuuint64_t) (n / 16), (cuuint64_t) (k / 16)};
         const cuuint64_t strides[2] = {(cuuint64_t) (32 * K), (cuuint64_t) (n / 16) * (cuuint64_t) (32 * K)};

@@ -62,6 +62,7 @@ constexpr int kNBImax = kMoeMaxInter / 128;
 constexpr int kNBHmax = kMoeMaxHidden / 128;
 // CTA roles: warps 0-7 consume (decode + MMA), warp 8 produces (tickets,
 // stage copies), warp 9 stores partials and runs the block epilogues.
+constexpr int kMoeClaimAhead = 4;    // ring stages still queued when the producer claims its next unit
 constexpr int kMoeConsumerWarps = 8;
 constexpr int kMoeProducerWarp = 8;
 constexpr int kMoeEpilogueWarp = 9;
@@ -111,12 +112,18 @@ static __device__ unsigned long long g_phase[PH_N];
 #define PHASE_COUNT(c) (ph_[c] += 1)
 #define PHASE_FLUSH(lane) do { ph_[PH_TOTAL] = clock64() - ph_start_; if ((lane) == 0) for (int i_ = 0; i_ < PH_N; ++i_) atomicAdd(&g_phase[i_], ph_[i_]); } while (0)
 #define PH_ARG , ph_[PH_DATA]
+// Per-CTA timeline (%globaltimer ns): entry, plan built, consumer warp 0 done
+// with its input items, consumer warp 0 / producer / epilogue leave their
+// loops, retire barrier passed, exit.
+static __device__ unsigned long long g_tl[320][8];
+#define TL_MARK(i) do { if ((threadIdx.x & 31) == 0) g_tl[blockIdx.x][i] = globaltimer_ns(); } while (0)
 #else
 #define PHASE_DECL
 #define PHASE_MARK(c)
 #define PHASE_COUNT(c)
 #define PHASE_FLUSH(lane)
 #define PH_ARG
+#define TL_MARK(i)
 #endif
 
 // Tensor maps: one 3-D map per (projection kind, K) describes an expert
@@ -429,23 +436,41 @@ __device__ void tp_finish_row(const MoeParams& p, uint32_t epoch, int blk, int r
 // Phase-B epilogue of (group g, hidden block blk), by one warp: sum the down
 // partials, output transform (lna_moe_ticket.cu:368-378); the last group to
 // finish block blk gathers it for every row in slot order (:409-428).
-__device__ void moe_finish_b(const MoeParams& p, const MoePlan& P, int g, int blk, int lane, uint32_t* cntG,
-                             uint32_t epoch, uint32_t* status) {
+// Phase-B block epilogue, part 1: the block's down output of every row of
+// group g -- the k-chunk partials summed in chunk order (or, with a single
+// chunk, the unit's tile straight from shared memory), out-H128 * svh -- into
+// downc.
+__device__ void moe_finish_b_rows(const MoeParams& p, const MoePlan& P, int g, int blk, int lane,
+                                  const float* tile) {
     const int e = P.gexp[g];
     const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
     const __half* dsv = reinterpret_cast<const __half*>(p.tab[8][e]) + blk * kCols;
     for (int ri = 0; ri < nrows; ++ri) {
         const int64_t pr = pair0 + ri;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c2 = 0; c2 < p.nkb; ++c2) {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(
-                p.partB + (pr * p.nkb + c2) * p.H + blk * kCols + lane * 4));
-            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        if (tile != nullptr) {
+            const float4 a = *reinterpret_cast<const float4*>(tile + ri * kCols + lane * 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        } else {
+            for (int c2 = 0; c2 < p.nkb; ++c2) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(
+                    p.partB + (pr * p.nkb + c2) * p.H + blk * kCols + lane * 4));
+                v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+            }
         }
         out_transform(v, dsv, lane);
         __stcg(reinterpret_cast<float4*>(p.downc + pr * p.H + blk * kCols + lane * 4),
                make_float4(v[0], v[1], v[2], v[3]));
     }
+}
+
+// Phase-B block epilogue, part 2: count the group's block as done; the last
+// group to finish hidden block blk gathers it for every row, the top-k slots
+// summed in slot order in fp32 (recipe-lna/lna2/lna_moe_ticket.cu:409-428).
+// The slots' rows are loaded eight at a time before any is summed, so their
+// L2 latencies overlap.
+__device__ void moe_finish_b_count(const MoeParams& p, const MoePlan& P, int blk, int lane, uint32_t* cntG,
+                                   uint32_t epoch) {
     __syncwarp();
     int last = 0;
     if (lane == 0) {
@@ -460,13 +485,24 @@ __device__ void moe_finish_b(const MoeParams& p, const MoePlan& P, int g, int bl
     if (!last) return;
     for (int r = 0; r < p.m; ++r) {
         float s[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k = 0; k < p.topk; ++k) {
-            const int pr = P.slotpair[r * p.topk + k];
-            if (pr >= 0) {
-                const float wv = p.weights[r * p.topk + k];
-                const float4 d = __ldcg(reinterpret_cast<const float4*>(
-                    p.downc + (int64_t) pr * p.H + blk * kCols + lane * 4));
-                s[0] += wv * d.x; s[1] += wv * d.y; s[2] += wv * d.z; s[3] += wv * d.w;
+        for (int k0 = 0; k0 < p.topk; k0 += 8) {
+            float4 d[8];
+            float wv[8];
+            bool ok[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int k = k0 + j;
+                const int pr = k < p.topk ? (int) P.slotpair[r * p.topk + k] : -1;
+                ok[j] = pr >= 0;
+                wv[j] = ok[j] ? p.weights[r * p.topk + k] : 0.f;
+                d[j] = __ldcg(reinterpret_cast<const float4*>(p.downc + (int64_t) (ok[j] ? pr : 0) * p.H +
+                                                               blk * kCols + lane * 4));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (ok[j]) {
+                    s[0] += wv[j] * d[j].x; s[1] += wv[j] * d[j].y; s[2] += wv[j] * d[j].z; s[3] += wv[j] * d[j].w;
+                }
             }
         }
         if (p.tp_world > 0) {
@@ -494,6 +530,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
     uint32_t* cntB = p.ctrl + kOffCntB;
     uint32_t* cntG = p.ctrl + kOffCntG;
 
+    if (tid == 0) TL_MARK(0);
     if (tid == 0) {
         S.tp_epoch = p.tp_world > 0 ? __ldcg(reinterpret_cast<const uint32_t*>(p.tp_bufs[p.tp_rank])) + 1u : 0u;
         for (int s = 0; s < p.ring.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kMoeConsumerWarps); }
@@ -502,6 +539,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         fence_barrier_init();
     }
     build_plan(S.plan, p, tid);     // ends with __syncthreads (also publishes the barrier init)
+    if (tid == 0) TL_MARK(1);
     const MoePlan& P = S.plan;
     const int G = P.G;
     const int NBI = p.I / kCols, NBH = p.H / kCols;
@@ -563,10 +601,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 ticket = claim_ticket(&p.ctrl[0], lane);
                 continue;
             }
-            // claim the next unit now; its atomic completes while this unit's
-            // stages are issued
-            int next_raw = 0;
-            if (lane == 0) next_raw = (int) atomicAdd(&p.ctrl[0], 1u);
             const int kind = d[0], g = d[1], mat = d[2], blk = d[3], s = d[4], K = d[5];
             const int e = P.gexp[g];
             const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
@@ -630,7 +664,24 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 ++it;
                 PHASE_MARK(PH_PROD_ISSUE);
             }
+            // Claim the next unit only once at most `ahead` stages of this CTA's
+            // ring are unconsumed: a CTA with a long backlog leaves the last
+            // tickets to idle CTAs instead of ending the layer late.  (Stage j is
+            // consumed when empty[j % ns] completes phase j / ns; ahead <= ns - 2
+            // keeps that phase the barrier's latest.)
+            int next_raw = total;
+            if (lane == 0 && ok) {
+                const uint32_t ns = (uint32_t) p.ring.ns;
+                const uint32_t ahead = min((uint32_t) kMoeClaimAhead, ns - 2u);
+                if (it > ahead) {
+                    const uint32_t j = it - ahead - 1u;
+                    ok = mbar_wait(&S.empty[j % ns], (j / ns) & 1u, status);
+                }
+                if (ok) next_raw = (int) atomicAdd(&p.ctrl[0], 1u);
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             ticket = __shfl_sync(0xffffffffu, next_raw, 0);
+            if (!ok) break;
         }
         // no bulk copy may still be writing shared memory when the CTA retires
         if (lane == 0) {
@@ -638,6 +689,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             for (uint32_t i = first; i < it; ++i)
                 if (!mbar_wait(&S.full[i % p.ring.ns], (i / p.ring.ns) & 1u, status)) break;
         }
+        TL_MARK(4);
         PHASE_FLUSH(lane);
     } else if (warp == kMoeEpilogueWarp) {
         // ------------------------------------------------------------ epilogue
@@ -663,6 +715,18 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             PHASE_MARK(PH_EPI_WAIT);
             const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
             const float* tile = ptile + (size_t) ps * p.m * kCols;
+            if (kind == 1 && p.nkb == 1) {
+                // A single k-chunk over I: the tile is the block's whole sum, so it
+                // is finished here without a partial store or a completion count.
+                PHASE_COUNT(PH_FINS_B);
+                moe_finish_b_rows(p, P, g, blk, lane, tile);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.pempty[ps]);
+                ++uu;
+                moe_finish_b_count(p, P, blk, lane, cntG, S.tp_epoch);
+                PHASE_MARK(PH_FIN_B);
+                continue;
+            }
             for (int r = 0; r < nrows; ++r) {
                 const float4 v = *reinterpret_cast<const float4*>(tile + r * kCols + lane * 4);
                 float* dst = kind == 0
@@ -700,10 +764,12 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 PHASE_MARK(PH_FIN_A);
             } else {
                 PHASE_COUNT(PH_FINS_B);
-                moe_finish_b(p, P, g, blk, lane, cntG, S.tp_epoch, status);
+                moe_finish_b_rows(p, P, g, blk, lane, nullptr);
+                moe_finish_b_count(p, P, blk, lane, cntG, S.tp_epoch);
                 PHASE_MARK(PH_FIN_B);
             }
         }
+        TL_MARK(5);
         PHASE_FLUSH(lane);
     } else {
         // ------------------------------------------------------------ consumers
@@ -727,6 +793,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             }
         }
         PHASE_MARK(PH_P);
+        if (warp == 0) TL_MARK(2);
 
         uint32_t it = 0, du = 0, uu = 0;
         const int t4 = lane & 3, gr = lane >> 2;
@@ -777,6 +844,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             ++uu;
             PHASE_MARK(PH_PARTIAL);
         }
+        if (warp == 0) TL_MARK(3);
         PHASE_FLUSH(lane);
     }
 
@@ -786,6 +854,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         __threadfence();
         const uint32_t old = atomicAdd(&p.ctrl[1], 1u);
         S.last_cta = old == gridDim.x - 1;
+        TL_MARK(6);
         S.retire_rank = (int) old;
     }
     __syncthreads();
@@ -799,6 +868,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         ok = __all_sync(0xffffffffu, ok);
         if (!ok && lane == 0) set_error(status, ERR_DEP_TIMEOUT);
     }
+    if (tid == 0) TL_MARK(7);
     if (S.last_cta) {
         __threadfence();
         for (int i = tid; i < G * 2 * kMoeMaxNka; i += kMoeThreads) readyP[i] = 0u;
@@ -1022,6 +1092,13 @@ extern "C" int exl3_phase_clock_read(unsigned long long* out, int n, int reset) 
     }
     return EXL3_OK;
 }
+
+extern "C" int exl3_timeline_read(unsigned long long* out, int n) {
+    EXL3_REQUIRE(out && n >= 1 && n <= 320 * 8, EXL3_ERR_ARG, "timeline: bad output");
+    EXL3_CUDA(cudaDeviceSynchronize());
+    EXL3_CUDA(cudaMemcpyFromSymbol(out, exl3::g_tl, sizeof(unsigned long long) * n));
+    return EXL3_OK;
+}
 #endif
 
 namespace exl3 {
@@ -1110,6 +1187,7 @@ int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_
     p.tp_world = tp.world;
     p.tp_mcap = (int) tp.mcap;
     ring_geom(m, k_table ? kmax : K, precise != 0, &p.ring.wpart, &p.ring.slot_bytes, &p.ring.ns);
+    shift_table_init(p.ring.st);
 
     const int smem = kMoeHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * (int) m * kCols * 4;
     auto s = static_cast<cudaStream_t>(stream);

@@ -25,6 +25,7 @@ struct RingGeom {
     int slot_bytes;           // bytes per stage
     int ns;                   // stages in the ring
     int wpart;                // weight part of a stage
+    ShiftTable st;            // IMAD shift multipliers of the window extraction (shift_table_init)
 };
 
 // B-fragment words per lane per row-slice: fast arithmetic keeps every
@@ -59,6 +60,11 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
 #pragma unroll
     for (int rb = 0; rb < RB; ++rb) boff[rb] = min(rb * 8 + gr, nrows - 1) * 4 * FW + t4 * FW;
     const int bstride = nrows * 4 * FW;                 // words per row-slice block of the unit
+    float acc_odd[RB][4];                               // odd-k MMAs (fast path), added to acc at the end
+#pragma unroll
+    for (int rb = 0; rb < RB; ++rb)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc_odd[rb][q] = 0.f;
     for (int st = 0; st < nst; ++st) {
         const int slot = (int) (it % (uint32_t) p.ns);
 #ifdef EXL3_PHASE_CLOCK
@@ -86,7 +92,7 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
                 wlo[h] = plo[h][i * ROWW];
             }
             uint32_t w[8], x[8];
-            tile_windows_w<K>(whi, wlo, geom, w);
+            tile_windows_f<K>(whi, wlo, geom, p.st, w);
 #pragma unroll
             for (int j = 0; j < 8; ++j) x[j] = codebook_pair<CB>(w[j]);
             const uint32_t* bs = bf + i * bstride;
@@ -95,13 +101,19 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
                 if constexpr (PRECISE) {
                     mma_tile_precise(acc[rb], x, *reinterpret_cast<const uint2*>(bs + boff[rb]));
                 } else {
-                    mma_tile(acc[rb], x, *reinterpret_cast<const uint4*>(bs + boff[rb]));
+                    mma_tile2(acc[rb], acc_odd[rb], x, *reinterpret_cast<const uint4*>(bs + boff[rb]));
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
         ++it;
+    }
+    if constexpr (!PRECISE) {
+#pragma unroll
+        for (int rb = 0; rb < RB; ++rb)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[rb][q] += acc_odd[rb][q];
     }
     return true;
 }
