@@ -328,6 +328,16 @@ class MoeWorkload:
     def bytes_per_step(self, i):
         return self.ubytes[i % len(self.layers)]
 
+    def weights_by_k(self):
+        """Mean weights per launch of this rank's shard, by bit width (unique
+        experts of each cycled layer, gate + up + down)."""
+        out: dict = {}
+        for L, (ids, _) in zip(self.layers, self.routes):
+            for e in self.torch.unique(ids).tolist():
+                k = int(L.kbits[e])
+                out[k] = out.get(k, 0.0) + 3.0 * self.H * self.I / len(self.layers)
+        return out
+
     launches_per_step = 1
     kernel_name = "exl3::moe_kernel"
     metric = None
@@ -641,6 +651,40 @@ def run_reference(args):
     }), flush=True)
 
 
+def decode_roof(weights_by_k: dict, kernel_us: float, dev) -> dict:
+    """Decode-issue roof of the launch: the layer's weights (per bit width)
+    over the rate of exl3_decode_roof -- the GEMV engine's decode loop on
+    shared-memory tiles, no HBM traffic -- timed here with CUDA events."""
+    import ctypes
+
+    import torch
+
+    from dsv4_carve_b200 import _lib
+
+    lib = _lib.load()
+    words = torch.randint(-2**31, 2**31 - 1, (32 * 8 * 8,), dtype=torch.int32, device=dev)
+    out = torch.empty(int(lib.exl3_decode_roof_out_floats()), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    rates = {}
+    for K in sorted(weights_by_k):
+        n = ctypes.c_int64(0)
+        args = (K, 1, 600, ctypes.c_void_p(words.data_ptr()), words.numel(), ctypes.c_void_p(out.data_ptr()),
+                out.numel(), ctypes.byref(n), ctypes.c_void_p(stream.cuda_stream))
+        _lib.check(lib.exl3_decode_roof(*args))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            _lib.check(lib.exl3_decode_roof(*args))
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        rates[K] = 5 * n.value / (e0.elapsed_time(e1) / 1e3)
+    roof_us = sum(w / rates[k] for k, w in weights_by_k.items()) * 1e6
+    return {"weights_per_launch": sum(weights_by_k.values()),
+            "weights_per_s": {str(k): v for k, v in rates.items()},
+            "layer_us": roof_us, "frac": roof_us / kernel_us, "codebook": "MCG",
+            "how": "exl3_decode_roof: the GEMV engine's decode loop on shared-memory tiles, 2 CTAs x 8 warps per SM"}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -778,6 +822,11 @@ def main():
         "e2e": e2e,
         "clocks": clock_info,
     }
+    if args.config == "moe" and hasattr(wl, "weights_by_k"):
+        try:
+            line["roofline"]["decode_roof"] = decode_roof(wl.weights_by_k(), kern_avg_ms * 1e3, dev)
+        except Exception as exc:   # the measurement aid must not void the bench line
+            line["roofline"]["decode_roof"] = {"error": repr(exc)}
     if world == 1 and not args.no_cpu and args.config == "moe":
         v, desc, cores, kind, dt, _ = cpu_reference_sample(args, args.cpu_seconds)
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc,

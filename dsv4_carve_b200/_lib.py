@@ -53,6 +53,8 @@ _SIGS = {
     "exl3_moe_prepare": (_I, [_I]),
     "exl3_moe_info": (_I, [_I, _P]),
     "exl3_scratch_status": (_I, [_P, _I, _I, _P, _P]),
+    "exl3_decode_roof_out_floats": (_I64, []),
+    "exl3_decode_roof": (_I, [_I, _I, _I, _P, _I64, _P, _I64, _P, _P]),
 }
 
 _lib = None

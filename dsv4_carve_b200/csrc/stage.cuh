@@ -65,12 +65,14 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
     for (int rb = 0; rb < RB; ++rb)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc_odd[rb][q] = 0.f;
+    // ring position as running counters (one division per unit, not per stage)
+    int slot = (int) (it % (uint32_t) p.ns);
+    uint32_t phase = (it / (uint32_t) p.ns) & 1u;
     for (int st = 0; st < nst; ++st) {
-        const int slot = (int) (it % (uint32_t) p.ns);
 #ifdef EXL3_PHASE_CLOCK
         const unsigned long long w0_ = clock64();
 #endif
-        if (!mbar_wait_lanes(&full[slot], (it / (uint32_t) p.ns) & 1u, status)) return false;
+        if (!mbar_wait_lanes(&full[slot], phase, status)) return false;
 #ifdef EXL3_PHASE_CLOCK
         ph_wait += clock64() - w0_;
 #endif
@@ -108,6 +110,7 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
         ++it;
+        if (++slot == p.ns) { slot = 0; phase ^= 1u; }
     }
     if constexpr (!PRECISE) {
 #pragma unroll

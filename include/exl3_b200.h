@@ -221,6 +221,21 @@ int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_dtype,
                      const int32_t* ids, const float* weights, int64_t topk,
                      float swiglu_limit, void* scratch, int64_t scratch_bytes, void* stream);
 
+/* Decode-issue roof: runs the GEMV engine's decode inner loop (window
+ * extraction, codebook, split-accumulator MMAs) on 32 weight tiles held in
+ * shared memory, with no global traffic, on a grid of 2 CTAs x 8 decoding
+ * warps per SM (the MoE kernel's occupancy), `iters` rounds of 8 k-slices per
+ * warp.  `words`: device uint32 [>= 32 * 8 * K], any bits (a tile's words);
+ * `out`: device float [>= exl3_decode_roof_out_floats()] (per-thread sums, so
+ * the work is not optimised away).  *weights_decoded receives the number of
+ * weights the launch decodes; time the launch on `stream` to get the rate.
+ * Counterpart of the reference's null-decode build, which removed the decode
+ * instead of the memory traffic (LNA2_NULL_DECODE,
+ * recipe-lna/lna2/lna_gemv_core.cuh:31-32,170). */
+int64_t exl3_decode_roof_out_floats(void);
+int exl3_decode_roof(int K, int cb, int iters, const void* words, int64_t words_len, float* out, int64_t out_len,
+                     int64_t* weights_decoded, void* stream);
+
 /* Device status word of a scratch buffer (MoE or linear): bit 0 dependency
  * wait timed out, bit 1 misaligned trellis pointer, bit 2 bit width out of
  * range, bit 3 ring wait timed out, bit 4 route plan overflow.  Synchronizes

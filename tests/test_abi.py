@@ -148,3 +148,15 @@ def test_python_layer_raises_without_cuda_tensors():
         ext.exl3_gemv(x, t, su, su, 2, True)
     with pytest.raises(RuntimeError, match="1 <= m <= 8"):
         ext.exl3_gemv(torch.zeros((9, 128), dtype=torch.float16), t, su, su, 2, True)
+
+
+def test_decode_roof_argument_checks():
+    lib = _lib.load()
+    n = C.c_int64(0)
+    buf = C.c_void_p(16)
+    for K, cb, iters in ((0, 1, 1), (9, 1, 1), (2, 2, 1), (2, 1, 0)):
+        assert lib.exl3_decode_roof(K, cb, iters, buf, 4096, buf, 1 << 20, C.byref(n), None) == _lib.EXL3_ERR_ARG
+    assert lib.exl3_decode_roof(2, 1, 1, None, 4096, buf, 1 << 20, C.byref(n), None) == _lib.EXL3_ERR_ARG
+    # too few tile words for K = 3 (32 tiles x 24 words)
+    assert lib.exl3_decode_roof(3, 1, 1, buf, 767, buf, 1 << 20, C.byref(n), None) == _lib.EXL3_ERR_ARG
+    assert "words" in _lib.last_error()
