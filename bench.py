@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--config", choices=["moe", "dense", "prefill"], default="moe",
                     help="moe: config 2/3 routed-MoE layer (the headline); dense: config 1 K6 linears")
     ap.add_argument("--rows", type=int, default=4, help="dense: activation rows R")
+    ap.add_argument("--group", action="store_true",
+                    help="dense: the two 4096-input matrices in one grouped launch (exl3_linear_group)")
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill: tokens per chunk")
     ap.add_argument("--emulate-tp", type=int, default=1,
                     help="one GPU: run rank 0's shard of a TP-N layer (intermediate / N), no collective")
@@ -489,6 +491,15 @@ class DenseWorkload:
         scratch_need = max(self.lib.exl3_linear_scratch_bytes(self.R, m.in_features, m.out_features, 6)
                            for mats in self.sets for m in mats)
         self.scratch = torch.zeros(scratch_need, dtype=torch.uint8, device=dev)
+        self._keep = []
+        if args.group:
+            import ctypes
+
+            m0 = self.sets[0]
+            gneed = self.lib.exl3_linear_group_scratch_bytes(
+                self.R, 4096, 2, (ctypes.c_int64 * 2)(m0[0].out_features, m0[1].out_features), 6)
+            self.gscratch = torch.zeros(gneed, dtype=torch.uint8, device=dev)
+            self.launches_per_step = 2
         x = synth.activations(self.R, 4096, seed=77, device=dev)
         for mats in self.sets:
             a, b, c = mats
@@ -500,6 +511,19 @@ class DenseWorkload:
                 argv.append((xi.data_ptr(), _lib.DT_F16, self.R, m.in_features, m.out_features, m.trellis.data_ptr(),
                              6, synth.CB_3INST, m.suh.data_ptr(), m.svh.data_ptr(), yo.data_ptr(), _lib.DT_F16,
                              self.scratch.data_ptr(), self.scratch.numel(), 1))
+            if args.group:
+                # [4096 -> 4096] and [4096 -> 1536] share x: one grouped launch
+                import ctypes
+
+                gn = (ctypes.c_int64 * 2)(a.out_features, b.out_features)
+                vp = lambda ts: (ctypes.c_void_p * 2)(*[t.data_ptr() for t in ts])   # noqa: E731
+                garr = (gn, vp([a.trellis, b.trellis]), vp([a.suh, b.suh]), vp([a.svh, b.svh]), vp(outs[:2]))
+                self._keep.append(garr)
+                argv = [("group", (x.data_ptr(), _lib.DT_F16, self.R, 4096, 2, garr[0], garr[1], 6, synth.CB_3INST,
+                                   garr[2], garr[3], garr[4], _lib.DT_F16, self.gscratch.data_ptr(),
+                                   self.gscratch.numel(), 1)), ("single", argv[2])]
+            else:
+                argv = [("single", a_) for a_ in argv]
             self.argv.append(argv)
             self.xs.append(ins)
             self.ys.append(outs)
@@ -511,8 +535,9 @@ class DenseWorkload:
         self.uniq = []
 
     def launch(self, i, stream_handle):
-        for a in self.argv[i % len(self.argv)]:
-            rc = self.lib.exl3_linear(*a, stream_handle)
+        for kind, a in self.argv[i % len(self.argv)]:
+            fn = self.lib.exl3_linear_group if kind == "group" else self.lib.exl3_linear
+            rc = fn(*a, stream_handle)
             if rc:
                 raise RuntimeError(self.lib.exl3_last_error().decode())
 
@@ -554,7 +579,8 @@ class DenseWorkload:
         return {"workload": "config1_dense_k6_linear_set", "rows": self.R, "K": 6, "codebook": "3INST",
                 "matrices": ["4096x4096", "4096x1536", "1536x4096"], "sets_cycled": len(self.sets),
                 "parallelism": f"tp{self.world}" if self.world > 1 else "single",
-                "l2": "sets cycled: 8 x 22 MB > 126 MB L2", "precise": True}
+                "l2": "sets cycled: 8 x 22 MB > 126 MB L2", "precise": True,
+                "grouped": bool(self.args.group)}
 
 
 # ----------------------------------------------------------------------------- CPU baseline

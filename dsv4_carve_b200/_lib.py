@@ -32,6 +32,8 @@ _SIGS = {
     "exl3_dequant": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _P, _I, _P]),
     "exl3_linear_scratch_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "exl3_linear": (_I, [_P, _I, _I64, _I64, _I64, _P, _I, _I, _P, _P, _P, _I, _P, _I64, _I, _P]),
+    "exl3_linear_group_scratch_bytes": (_I64, [_I64, _I64, _I, _P, _I]),
+    "exl3_linear_group": (_I, [_P, _I, _I64, _I64, _I, _P, _P, _I, _I, _P, _P, _P, _I, _P, _I64, _I, _P]),
     "exl3_moe_scratch_bytes": (_I64, [_I64, _I64, _I64, _I64]),
     "exl3_moe_max_rows": (_I64, []),
     "exl3_moe_decode": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9

@@ -121,26 +121,33 @@ constexpr int kLinMaxChunks = 8;             // k-chunks per 128-column block
 constexpr int kLinRingBytes = 98304;         // ring + partial tiles
 constexpr int kLinMaxStages = 12;
 constexpr int kLinDQ = 4;
+constexpr int kLinMaxMats = 8;               // matrices of one grouped launch (shared input)
 // control words: [0] unit ticket [1] retired CTAs [2] status [3] input items,
-// readyP[kLinMaxChunks] at 16, block counters at 16 + kLinMaxChunks
+// readyP[matrix][chunk] at 16, block counters (over all matrices' 128-column
+// blocks) after them
 constexpr int kLinOffReady = 16;
-constexpr int kLinOffCnt = kLinOffReady + kLinMaxChunks;
+constexpr int kLinOffCnt = kLinOffReady + kLinMaxMats * kLinMaxChunks;
 
+// One launch applies nmat matrices (same k, K and codebook) to the same input
+// rows: matrix j has its own trellis map, suh, svh, width n[j] and output
+// y[j]; its 128-column blocks are blocks blk0[j] .. blk0[j+1]-1 of the launch.
 struct LinearParams {
-    CUtensorMap tmap;           // trellis as [k/16][n/16][16K] u16, box [16K, 8, SK]
+    CUtensorMap tmap[kLinMaxMats];   // trellis as [k/16][n/16][16K] u16, box [16K, 8, SK]
     const void* x;
     int x_dtype;
     int rows;
-    int k, n;
-    const __half* suh;
-    const __half* svh;
-    void* y;
+    int k, nmat, ntot;               // ntot = sum of n[j] (row stride of the partials)
+    int n[kLinMaxMats];
+    int blk0[kLinMaxMats + 1];
+    const __half* suh[kLinMaxMats];
+    const __half* svh[kLinMaxMats];
+    void* y[kLinMaxMats];
     int y_dtype;
     int kc, nk;                 // k-chunk per unit, chunk count
     RingGeom ring;
     uint32_t* ctrl;
-    uint32_t* xg;               // B fragments [k/16][rows][4][FW]
-    float* partial;             // [nk][rows][n]
+    uint32_t* xg;               // B fragments [nmat][k/16][rows][4][FW]
+    float* partial;             // [nk][rows][ntot]
 };
 
 struct alignas(128) LinHead {
@@ -166,8 +173,9 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
     uint32_t* status = p.ctrl + 2;
     uint32_t* readyP = p.ctrl + kLinOffReady;
     uint32_t* cnt = p.ctrl + kLinOffCnt;
-    const int NB = p.n / kCols;
+    const int NB = p.blk0[p.nmat];
     const int total = NB * p.nk;
+    const int64_t xg_mat = (int64_t) (p.k / 16) * p.rows * 4 * FW;   // fragment words per matrix
     const int rows = p.rows;
 
     if (tid == 0) {
@@ -189,7 +197,9 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
         const int nst = p.kc / (16 * kStageSK);
         while (ok) {
             const bool end = ticket >= total;
-            const int blk = end ? 0 : ticket / p.nk, s = end ? 0 : ticket % p.nk;
+            const int blk = end ? 0 : ticket / p.nk, s = end ? 0 : ticket % p.nk;   // blk over all matrices
+            int mat = 0;
+            while (mat + 1 < p.nmat && blk >= p.blk0[mat + 1]) ++mat;
             int next_raw = 0;
             if (!end && lane == 0) next_raw = (int) atomicAdd(&p.ctrl[0], 1u);
             if (lane == 0) {
@@ -206,12 +216,12 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             ++du;
             if (end || !ok) break;
             if (lane == 0) {
-                wait_counter(&readyP[s], (uint32_t) (p.kc / kCols * rows), status);
+                wait_counter(&readyP[mat * kLinMaxChunks + s], (uint32_t) (p.kc / kCols * rows), status);
                 fence_proxy_async_global();
             }
             __syncwarp();
             const int ks0 = s * (p.kc / 16);
-            const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.xg) + (int64_t) ks0 * rsb;
+            const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.xg + mat * xg_mat) + (int64_t) ks0 * rsb;
             for (int st = 0; st < nst && ok; ++st) {
                 const int slot = (int) (it % (uint32_t) p.ring.ns);
                 if (lane == 0) {
@@ -219,7 +229,8 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
                     if (ok) {
                         uint8_t* dst = ring + (size_t) slot * p.ring.slot_bytes;
                         mbar_arrive_expect_tx(&S.full[slot], wbytes + (uint32_t) bbytes);
-                        tma_load_3d(dst, &p.tmap, 0, blk * 8, ks0 + st * kStageSK, &S.full[slot]);
+                        tma_load_3d(dst, &p.tmap[mat], 0, (blk - p.blk0[mat]) * 8, ks0 + st * kStageSK,
+                                    &S.full[slot]);
                         bulk_g2s(dst + p.ring.wpart, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
                     }
                 }
@@ -251,7 +262,8 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             const float* tile = ptile + (size_t) ps * rows * kCols;
             for (int r = 0; r < rows; ++r) {
                 const float4 v = *reinterpret_cast<const float4*>(tile + r * kCols + lane * 4);
-                __stcg(reinterpret_cast<float4*>(p.partial + ((int64_t) s * rows + r) * p.n + blk * kCols + lane * 4), v);
+                __stcg(reinterpret_cast<float4*>(p.partial + ((int64_t) s * rows + r) * p.ntot + blk * kCols + lane * 4),
+                       v);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.pempty[ps]);
@@ -267,6 +279,9 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             }
             last = __shfl_sync(0xffffffffu, last, 0);
             if (!last) continue;
+            int mat = 0;
+            while (mat + 1 < p.nmat && blk >= p.blk0[mat + 1]) ++mat;
+            const int lb = blk - p.blk0[mat];   // the block within its matrix
             for (int r = 0; r < rows; ++r) {
                 // all chunk partials of the row in flight at once, summed in chunk order
                 float4 a[kLinMaxChunks];
@@ -274,27 +289,30 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
                 for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
                     if (c2 < p.nk)
                         a[c2] = __ldcg(reinterpret_cast<const float4*>(
-                            p.partial + ((int64_t) c2 * rows + r) * p.n + blk * kCols + lane * 4));
+                            p.partial + ((int64_t) c2 * rows + r) * p.ntot + blk * kCols + lane * 4));
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
                     if (c2 < p.nk) { v[0] += a[c2].x; v[1] += a[c2].y; v[2] += a[c2].z; v[3] += a[c2].w; }
-                out_transform(v, p.svh + blk * kCols, lane);
+                out_transform(v, p.svh[mat] + lb * kCols, lane);
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    store_out(p.y, p.y_dtype, (int64_t) r * p.n + blk * kCols + lane * 4 + q, v[q]);
+                    store_out(p.y[mat], p.y_dtype, (int64_t) r * p.n[mat] + lb * kCols + lane * 4 + q, v[q]);
             }
         }
     } else {
         // ------------------------------------------------------------ consumers
-        // input transform: one (128-block of k, row) per item; a block's
-        // fragments are ready when all its rows are
+        // input transform: one (matrix, 128-block of k, row) per item (each
+        // matrix has its own suh); a block's fragments are ready when all its
+        // rows are
         const int KB = p.k / kCols;
         while (true) {
             int item = 0;
             if (lane == 0) item = (int) atomicAdd(&p.ctrl[3], 1u);
             item = __shfl_sync(0xffffffffu, item, 0);
-            if (item >= KB * rows) break;
+            if (item >= p.nmat * KB * rows) break;
+            const int mat = item / (KB * rows);
+            item -= mat * KB * rows;
             const int r = item % rows;
             item /= rows;
             const int k0 = item * kCols + lane * 4;
@@ -303,21 +321,21 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const __half a = load_act_half(p.x, p.x_dtype, (int64_t) r * p.k + k0 + q);
-                    v[q] = __half2float(__hmul(a, p.suh[k0 + q]));
+                    v[q] = __half2float(__hmul(a, p.suh[mat][k0 + q]));
                 }
                 wht128_warp(v, lane);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const int kl = lane * 4 + q;
                     const int ks = item * 8 + (kl >> 4);
-                    store_frag<PRECISE>(p.xg + ((size_t) ks * rows + r) * 4 * FW, kl & 15,
+                    store_frag<PRECISE>(p.xg + mat * xg_mat + ((size_t) ks * rows + r) * 4 * FW, kl & 15,
                                         __float2half_rn(v[q] * kHadNorm));
                 }
             }
             __syncwarp();
             if (lane == 0) {
                 fence_proxy_async_global();
-                atom_add_release_gpu(&readyP[item / (p.kc / kCols)], 1u);
+                atom_add_release_gpu(&readyP[mat * kLinMaxChunks + item / (p.kc / kCols)], 1u);
             }
         }
         uint32_t it = 0, du = 0, uu = 0;
@@ -372,7 +390,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
     __syncthreads();
     if (S.last_cta) {
         __threadfence();
-        for (int i = tid; i < p.nk; i += kLinThreads) readyP[i] = 0u;
+        for (int i = tid; i < p.nmat * kLinMaxChunks; i += kLinThreads) readyP[i] = 0u;
         if (tid == 0) {
             atomicExch(&p.ctrl[0], 0u);
             atomicExch(&p.ctrl[3], 0u);
@@ -554,18 +572,36 @@ extern "C" int exl3_dequant(const void* trellis, int64_t kt, int64_t nt, int K, 
     return EXL3_OK;
 }
 
-// Scratch: control words, the input fragments (sized for 4-word fragments)
-// and the chunk partials.
-static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t n, int grid) {
-    const int nk = pick_chunks(k, n, grid);
-    return EXL3_LINEAR_CTRL_BYTES + align_up(k * rows_blk * 4, 256) + align_up((int64_t) nk * rows_blk * n * 4, 256);
+// Scratch: control words, the input fragments of every matrix (sized for
+// 4-word fragments) and the chunk partials over all matrices' columns.
+static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t ntot, int nmat, int grid) {
+    const int nk = pick_chunks(k, ntot, grid);
+    return EXL3_LINEAR_CTRL_BYTES + align_up((int64_t) nmat * k * rows_blk * 4, 256) +
+           align_up((int64_t) nk * rows_blk * ntot * 4, 256);
 }
 
-// Scratch for `rows` rows: the tensor-core path's (>= 64 rows) or the GEMV path's.
-static int64_t linear_need(int64_t rows, int64_t k, int64_t n, int grid) {
-    if (linear_tc_eligible(rows, k, n)) return linear_tc_scratch_bytes(rows, k, n);
+// Scratch for `rows` rows: the tensor-core path's (>= 64 rows, one matrix at a
+// time) or the GEMV path's.
+static int64_t linear_group_need(int64_t rows, int64_t k, int nmat, const int64_t* n, int grid) {
+    int64_t ntot = 0, tc = 0;
+    bool all_tc = true;
+    for (int j = 0; j < nmat; ++j) {
+        ntot += n[j];
+        if (linear_tc_eligible(rows, k, n[j])) {
+            const int64_t b = linear_tc_scratch_bytes(rows, k, n[j]);
+            tc = b > tc ? b : tc;
+        } else {
+            all_tc = false;
+        }
+    }
+    if (all_tc) return tc;
     const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
-    return linear_scratch_for(rb, k, n, grid);
+    const int64_t g = linear_scratch_for(rb, k, ntot, nmat, grid);
+    return g > tc ? g : tc;
+}
+
+static int64_t linear_need(int64_t rows, int64_t k, int64_t n, int grid) {
+    return linear_group_need(rows, k, 1, &n, grid);
 }
 
 extern "C" int64_t exl3_linear_scratch_bytes(int64_t rows, int64_t k, int64_t n, int K) {
@@ -573,61 +609,103 @@ extern "C" int64_t exl3_linear_scratch_bytes(int64_t rows, int64_t k, int64_t n,
     return linear_need(rows, k, n, assumed_grid());
 }
 
-extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis,
-                           int K, int cb, const void* suh, const void* svh, void* y, int y_dtype, void* scratch,
-                           int64_t scratch_bytes, int precise, void* stream) {
-    EXL3_REQUIRE(x && trellis && suh && svh && y && scratch, EXL3_ERR_ARG, "exl3_linear: null pointer argument");
-    EXL3_REQUIRE(rows >= 1, EXL3_ERR_ARG, "exl3_linear: rows must be >= 1");
-    EXL3_REQUIRE(k % 128 == 0 && n % 128 == 0 && k > 0 && n > 0, EXL3_ERR_ARG,
-                 "exl3_linear: k and n must be positive multiples of 128 (got %lld, %lld)", (long long) k,
-                 (long long) n);
-    EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_ARG, "exl3_linear: K must be in 1..8 (got %d)", K);
-    EXL3_REQUIRE(cb >= 0 && cb <= 2, EXL3_ERR_ARG, "exl3_linear: codebook must be 0, 1 or 2");
+extern "C" int64_t exl3_linear_group_scratch_bytes(int64_t rows, int64_t k, int nmat, const int64_t* n, int K) {
+    if (rows < 1 || k < 128 || nmat < 1 || nmat > kLinMaxMats || !n || K < 1 || K > 8) return -1;
+    for (int j = 0; j < nmat; ++j)
+        if (n[j] < 128) return -1;
+    return linear_group_need(rows, k, nmat, n, assumed_grid());
+}
+
+namespace exl3 {
+namespace {
+
+// The GEMV engine over a group of nmat matrices sharing x (checked by the
+// callers): one launch per block of 32 rows.  Matrices that the tensor-core
+// path takes (>= 64 rows) run one after another on it instead.
+int linear_group_impl(const char* who, const void* x, int x_dtype, int64_t rows, int64_t k, int nmat,
+                      const int64_t* n, const void* const* trellis, int K, int cb, const void* const* suh,
+                      const void* const* svh, void* const* y, int y_dtype, void* scratch, int64_t scratch_bytes,
+                      int precise, void* stream) {
+    EXL3_REQUIRE(x && scratch && n && trellis && suh && svh && y, EXL3_ERR_ARG, "%s: null pointer argument", who);
+    EXL3_REQUIRE(nmat >= 1 && nmat <= kLinMaxMats, EXL3_ERR_ARG, "%s: 1 to %d matrices (got %d)", who, kLinMaxMats,
+                 nmat);
+    EXL3_REQUIRE(rows >= 1, EXL3_ERR_ARG, "%s: rows must be >= 1", who);
+    EXL3_REQUIRE(k % 128 == 0 && k > 0, EXL3_ERR_ARG, "%s: k and n must be positive multiples of 128 (k = %lld)",
+                 who, (long long) k);
+    EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_ARG, "%s: K must be in 1..8 (got %d)", who, K);
+    EXL3_REQUIRE(cb >= 0 && cb <= 2, EXL3_ERR_ARG, "%s: codebook must be 0, 1 or 2", who);
     EXL3_REQUIRE(x_dtype >= 0 && x_dtype <= 2 && y_dtype >= 0 && y_dtype <= 2, EXL3_ERR_ARG,
-                 "exl3_linear: dtype codes are 0 (fp16), 1 (bf16), 2 (fp32)");
-    EXL3_REQUIRE(aligned16(trellis), EXL3_ERR_ARG, "exl3_linear: trellis must be 16-byte aligned");
-    EXL3_REQUIRE(aligned16(scratch), EXL3_ERR_ARG, "exl3_linear: scratch must be 16-byte aligned");
-    EXL3_REQUIRE(n / 128 + kLinOffCnt <= EXL3_LINEAR_CTRL_BYTES / 4,
-                 EXL3_ERR_UNSUPPORTED, "exl3_linear: n too large");
+                 "%s: dtype codes are 0 (fp16), 1 (bf16), 2 (fp32)", who);
+    EXL3_REQUIRE(aligned16(scratch), EXL3_ERR_ARG, "%s: scratch must be 16-byte aligned", who);
+    int64_t ntot = 0;
+    for (int j = 0; j < nmat; ++j) {
+        EXL3_REQUIRE(trellis[j] && suh[j] && svh[j] && y[j], EXL3_ERR_ARG, "%s: null pointer for matrix %d", who, j);
+        EXL3_REQUIRE(n[j] % 128 == 0 && n[j] > 0, EXL3_ERR_ARG,
+                     "%s: k and n must be positive multiples of 128 (matrix %d: n = %lld)", who, j, (long long) n[j]);
+        EXL3_REQUIRE(aligned16(trellis[j]), EXL3_ERR_ARG, "%s: trellis must be 16-byte aligned", who);
+        ntot += n[j];
+    }
+    EXL3_REQUIRE(ntot / 128 + kLinOffCnt <= EXL3_LINEAR_CTRL_BYTES / 4, EXL3_ERR_UNSUPPORTED, "%s: n too large", who);
     const int grid = assumed_grid();
     const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
-    const int64_t need = linear_need(rows, k, n, grid);
-    EXL3_REQUIRE(scratch_bytes >= need, EXL3_ERR_ARG, "exl3_linear: scratch too small (%lld < %lld bytes)",
+    const int64_t need = linear_group_need(rows, k, nmat, n, grid);
+    EXL3_REQUIRE(scratch_bytes >= need, EXL3_ERR_ARG, "%s: scratch too small (%lld < %lld bytes)", who,
                  (long long) scratch_bytes, (long long) need);
-    if (linear_tc_eligible(rows, k, n))
-        return linear_tc(x, x_dtype, rows, k, n, trellis, K, cb, suh, svh, y, y_dtype, scratch,
-                         static_cast<cudaStream_t>(stream));
+    auto s = static_cast<cudaStream_t>(stream);
+    // matrices for the tensor-core path, one launch sequence each
+    int gm = 0;
+    int64_t gn[kLinMaxMats];
+    const void* gt[kLinMaxMats];
+    const void* gsu[kLinMaxMats];
+    const void* gsv[kLinMaxMats];
+    void* gy[kLinMaxMats];
+    for (int j = 0; j < nmat; ++j) {
+        if (linear_tc_eligible(rows, k, n[j])) {
+            if (int rc = linear_tc(x, x_dtype, rows, k, n[j], trellis[j], K, cb, suh[j], svh[j], y[j], y_dtype, scratch,
+                                   s))
+                return rc;
+        } else {
+            gn[gm] = n[j]; gt[gm] = trellis[j]; gsu[gm] = suh[j]; gsv[gm] = svh[j]; gy[gm] = y[j];
+            ++gm;
+        }
+    }
+    if (gm == 0) return EXL3_OK;
     auto encode = tmap_encoder();
-    EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "exl3_linear: cuTensorMapEncodeTiled is not available");
+    EXL3_REQUIRE(encode != nullptr, EXL3_ERR_CUDA, "%s: cuTensorMapEncodeTiled is not available", who);
 
     LinearParams p{};
     shift_table_init(p.ring.st);
-    {
-        const cuuint64_t dims[3] = {(cuuint64_t) (16 * K), (cuuint64_t) (n / 16), (cuuint64_t) (k / 16)};
-        const cuuint64_t strides[2] = {(cuuint64_t) (32 * K), (cuuint64_t) (n / 16) * (cuuint64_t) (32 * K)};
+    int64_t gtot = 0;
+    for (int j = 0; j < gm; ++j) {
+        const cuuint64_t dims[3] = {(cuuint64_t) (16 * K), (cuuint64_t) (gn[j] / 16), (cuuint64_t) (k / 16)};
+        const cuuint64_t strides[2] = {(cuuint64_t) (32 * K), (cuuint64_t) (gn[j] / 16) * (cuuint64_t) (32 * K)};
         const cuuint32_t box[3] = {(cuuint32_t) (16 * K), 8u, (cuuint32_t) kStageSK};
         const cuuint32_t estr[3] = {1u, 1u, 1u};
-        const CUresult r = encode(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(trellis), dims,
+        const CUresult r = encode(&p.tmap[j], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(gt[j]), dims,
                                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        EXL3_REQUIRE(r == CUDA_SUCCESS, EXL3_ERR_CUDA, "exl3_linear: cuTensorMapEncodeTiled failed (%d)", (int) r);
+        EXL3_REQUIRE(r == CUDA_SUCCESS, EXL3_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", who, (int) r);
+        p.n[j] = (int) gn[j];
+        p.blk0[j] = (int) (gtot / kCols);
+        p.suh[j] = static_cast<const __half*>(gsu[j]);
+        p.svh[j] = static_cast<const __half*>(gsv[j]);
+        gtot += gn[j];
     }
+    p.blk0[gm] = (int) (gtot / kCols);
+    p.nmat = gm;
+    p.ntot = (int) gtot;
     p.k = (int) k;
-    p.n = (int) n;
-    p.suh = static_cast<const __half*>(suh);
-    p.svh = static_cast<const __half*>(svh);
     p.x_dtype = x_dtype;
     p.y_dtype = y_dtype;
-    p.nk = pick_chunks(k, n, grid);
+    p.nk = pick_chunks(k, gtot, grid);
     p.kc = (int) (k / p.nk);
     uint8_t* sb = static_cast<uint8_t*>(scratch);
     p.ctrl = reinterpret_cast<uint32_t*>(sb);
     p.xg = reinterpret_cast<uint32_t*>(sb + EXL3_LINEAR_CTRL_BYTES);
-    p.partial = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES + align_up(k * rb * 4, 256));
+    p.partial = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES + align_up((int64_t) gm * k * rb * 4, 256));
     const int fw = precise ? 2 : 4;
     const int esz_x = x_dtype == 2 ? 4 : 2, esz_y = y_dtype == 2 ? 4 : 2;
-    const int64_t units = (n / kCols) * p.nk;
-    auto s = static_cast<cudaStream_t>(stream);
+    const int64_t units = (gtot / kCols) * p.nk;
     for (int64_t r0 = 0; r0 < rows; r0 += kLinMaxRows) {
         p.rows = (int) ((rows - r0) < kLinMaxRows ? (rows - r0) : kLinMaxRows);
         p.ring.wpart = kStageSK * 8 * 32 * K;
@@ -636,10 +714,32 @@ extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, 
         const int nsl = budget / p.ring.slot_bytes;
         p.ring.ns = nsl < 2 ? 2 : (nsl > kLinMaxStages ? kLinMaxStages : nsl);
         const int smem = kLinHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * p.rows * kCols * 4;
-        EXL3_REQUIRE(smem <= kLinHeadBytes + kLinRingBytes, EXL3_ERR_UNSUPPORTED, "exl3_linear: stage too large");
+        EXL3_REQUIRE(smem <= kLinHeadBytes + kLinRingBytes, EXL3_ERR_UNSUPPORTED, "%s: stage too large", who);
         p.x = static_cast<const uint8_t*>(x) + r0 * k * esz_x;
-        p.y = static_cast<uint8_t*>(y) + r0 * n * esz_y;
+        for (int j = 0; j < gm; ++j) p.y[j] = static_cast<uint8_t*>(gy[j]) + r0 * gn[j] * esz_y;
         if (int rc = launch_linear_any(K, cb, precise != 0, p, (int) units, smem, s)) return rc;
     }
     return EXL3_OK;
 }
+
+}  // namespace
+}  // namespace exl3
+
+extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis,
+                           int K, int cb, const void* suh, const void* svh, void* y, int y_dtype, void* scratch,
+                           int64_t scratch_bytes, int precise, void* stream) {
+    EXL3_REQUIRE(x && trellis && suh && svh && y && scratch, EXL3_ERR_ARG, "exl3_linear: null pointer argument");
+    EXL3_REQUIRE(n % 128 == 0 && n > 0, EXL3_ERR_ARG, "exl3_linear: k and n must be positive multiples of 128 (got %lld, %lld)",
+                 (long long) k, (long long) n);
+    return linear_group_impl("exl3_linear", x, x_dtype, rows, k, 1, &n, &trellis, K, cb, &suh, &svh, &y, y_dtype,
+                             scratch, scratch_bytes, precise, stream);
+}
+
+extern "C" int exl3_linear_group(const void* x, int x_dtype, int64_t rows, int64_t k, int nmat, const int64_t* n,
+                                 const void* const* trellis, int K, int cb, const void* const* suh,
+                                 const void* const* svh, void* const* y, int y_dtype, void* scratch,
+                                 int64_t scratch_bytes, int precise, void* stream) {
+    return linear_group_impl("exl3_linear_group", x, x_dtype, rows, k, nmat, n, trellis, K, cb, suh, svh, y, y_dtype,
+                             scratch, scratch_bytes, precise, stream);
+}
+

@@ -25,7 +25,7 @@ import torch
 from . import _lib
 
 __all__ = [
-    "dequant_trellis", "exl3_gemv", "exl3_gemm", "lna2_moe_decode", "lna2_moe_scratch_bytes",
+    "dequant_trellis", "exl3_gemv", "exl3_gemm", "exl3_mgemm", "lna2_moe_decode", "lna2_moe_scratch_bytes",
     "lna2_moe_max_rows", "lna2_moe_prepare", "lna2_moe_info", "lna2_moe_status",
     "exl3_linear_scratch_bytes",
 ]
@@ -136,6 +136,48 @@ def linear_forward(x2: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, s
                   suh.data_ptr(), svh.data_ptr(), y.data_ptr(), _DT[out_dtype], scratch.data_ptr(),
                   scratch.numel(), int(bool(precise)), _stream(x2.device))
     return y
+
+
+def linear_group_forward(x2: torch.Tensor, mats: list, K: int, codebook: int, out_dtype: torch.dtype,
+                         precise: bool = True) -> list:
+    """[x2 . W_j for each (trellis_j, suh_j, svh_j) in mats] in one launch:
+    one input, up to 8 matrices of the same k, bit width and codebook
+    (exllamav3_ext.exl3_mgemm with a broadcast input,
+    recipe-lna/exllamav3/exl3_gemm.cu.lna:659-679)."""
+    import ctypes
+
+    m, k = x2.shape
+    nm = len(mats)
+    _check(1 <= nm <= 8, "exl3 linear group: 1 to 8 matrices")
+    _check(x2.dtype in _DT and out_dtype in _DT, "exl3 linear: dtypes must be fp16, bf16 or fp32")
+    for t, su, sv in mats:
+        _linear_checks(x2, t, su, sv, K)
+    ns = [int(t.size(1)) * 16 for t, _, _ in mats]
+    ys = [torch.empty((m, n), dtype=out_dtype, device=x2.device) for n in ns]
+    arr_n = (ctypes.c_int64 * nm)(*ns)
+    ptrs = lambda ts: (ctypes.c_void_p * nm)(*[t.data_ptr() for t in ts])   # noqa: E731
+    lib = _lib.load()
+    nbytes = int(lib.exl3_linear_group_scratch_bytes(m, k, nm, arr_n, K))
+    _check(nbytes > 0, "exl3 linear group: unsupported shape")
+    scratch = _linear_scratch(x2.device, nbytes)
+    with _on_device(x2.device):
+        _lib.check(lib.exl3_linear_group(x2.data_ptr(), _DT[x2.dtype], m, k, nm, arr_n,
+                                         ptrs([t for t, _, _ in mats]), K, codebook, ptrs([su for _, su, _ in mats]),
+                                         ptrs([sv for _, _, sv in mats]), ptrs(ys), _DT[out_dtype],
+                                         scratch.data_ptr(), scratch.numel(), int(bool(precise)), _stream(x2.device)))
+    return ys
+
+
+def exl3_mgemm(x: torch.Tensor, trellis: list, suh: list, svh: list, K: int, mcg: bool, *,
+               codebook: int | None = None, out_dtype: torch.dtype = torch.float32) -> list:
+    """Grouped EXL3 GEMM over matrices sharing the input x [..., k]: returns
+    one [m, n_j] output per matrix (fp32 by default, as the plugin's dense
+    groups use it, recipe-lna/vllm_exl3_exl3.py.lna:546-613)."""
+    bits = int(K)
+    _check(len(trellis) == len(suh) == len(svh), "exl3_mgemm: trellis, suh and svh lists differ in length")
+    x2 = x.contiguous().view(x.numel() // x.size(-1), x.size(-1))
+    mats = [(t.contiguous(), su.contiguous(), sv.contiguous()) for t, su, sv in zip(trellis, suh, svh)]
+    return linear_group_forward(x2, mats, bits, _codebook(mcg, codebook), out_dtype)
 
 
 def _linear_checks(x, trellis, suh, svh, bits):

@@ -86,6 +86,26 @@ int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n,
                 void* y, int y_dtype, void* scratch, int64_t scratch_bytes, int precise,
                 void* stream);
 
+/* Grouped dense linear: nmat (1..8) EXL3 matrices applied to the same input
+ * rows in one launch, y_j[rows, n[j]] = x[rows, k] . W_j -- every matrix with
+ * its own trellis [k/16, n[j]/16, 16K], suh [k], svh [n[j]] and output y[j]
+ * (row-major, leading dimension n[j]); one k, K and codebook for the group.
+ * Replaces exllamav3_ext.exl3_mgemm with a broadcast input (bszm_in = 1,
+ * per-matrix suh / svh / width / output pointer:
+ * recipe-lna/exllamav3/exl3_gemm.cu.lna:659-679, called by the plugin's
+ * dense groups at recipe-lna/vllm_exl3_exl3.py.lna:546-613).  The k-chunked
+ * units of all matrices share one ticket counter, so a group of small
+ * matrices fills the GPU like one wide matrix.  Matrices that take the
+ * tensor-core path (>= 64 rows) run one after another on it.  `scratch`:
+ * >= exl3_linear_group_scratch_bytes(rows, k, nmat, n, K) bytes, first
+ * EXL3_LINEAR_CTRL_BYTES zero before first use (left zero); sum of n[j] up to
+ * 120,832.  `n`, `trellis`, `suh`, `svh` and `y` are host arrays of nmat
+ * entries (device addresses in the pointer arrays). */
+int64_t exl3_linear_group_scratch_bytes(int64_t rows, int64_t k, int nmat, const int64_t* n, int K);
+int exl3_linear_group(const void* x, int x_dtype, int64_t rows, int64_t k, int nmat, const int64_t* n,
+                      const void* const* trellis, int K, int cb, const void* const* suh, const void* const* svh,
+                      void* const* y, int y_dtype, void* scratch, int64_t scratch_bytes, int precise, void* stream);
+
 /* ------------------------------------------------------------------ routed MoE
  * One routed-expert decode layer on one rank (TP shard of the intermediate
  * dim): for every valid (row, slot), expert e = ids[row, slot]:

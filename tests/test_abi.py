@@ -160,3 +160,31 @@ def test_decode_roof_argument_checks():
     # too few tile words for K = 3 (32 tiles x 24 words)
     assert lib.exl3_decode_roof(3, 1, 1, buf, 767, buf, 1 << 20, C.byref(n), None) == _lib.EXL3_ERR_ARG
     assert "words" in _lib.last_error()
+
+
+def test_linear_group_argument_checks():
+    lib = _lib.load()
+    buf = (C.c_uint8 * 64)()
+    p = C.addressof(buf)
+    ptr = lambda *v: (C.c_void_p * len(v))(*v)   # noqa: E731
+    n2 = (C.c_int64 * 2)(128, 256)
+    t2, s2 = ptr(p, p), ptr(p, p)
+
+    def call(nmat=2, n=n2, t=t2, rows=1, k=128, K=2, cb=1, x=p, scratch_bytes=1 << 30):
+        return lib.exl3_linear_group(x, 0, rows, k, nmat, n, t, K, cb, s2, s2, s2, 0, p, scratch_bytes, 1, None)
+
+    _err(call(x=None), "null pointer")
+    _err(call(nmat=0), "1 to 8 matrices")
+    _err(call(nmat=9), "1 to 8 matrices")
+    _err(call(rows=0), "rows must be")
+    _err(call(k=100), "multiples of 128")
+    _err(call(n=(C.c_int64 * 2)(128, 200)), "matrix 1")
+    _err(call(t=ptr(p, p + 2)), "16-byte aligned")
+    _err(call(t=ptr(p, None)), "matrix 1")
+    _err(call(K=0), "K must be")
+    _err(call(scratch_bytes=64), "scratch too small")
+    assert lib.exl3_linear_group_scratch_bytes(4, 1024, 2, n2, 3) > _lib.LINEAR_CTRL_BYTES
+    assert lib.exl3_linear_group_scratch_bytes(4, 1024, 9, n2, 3) == -1
+    assert lib.exl3_linear_group_scratch_bytes(4, 1024, 2, (C.c_int64 * 2)(128, 100), 3) == -1
+    one = (C.c_int64 * 1)(4096)
+    assert lib.exl3_linear_group_scratch_bytes(4, 4096, 1, one, 6) == lib.exl3_linear_scratch_bytes(4, 4096, 4096, 6)
