@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--stack", action="store_true",
+                    help="moe: config 4(a), the decode layer stack (every 8th layer all-K2); a step is one layer, "
+                         "the line adds the whole stack's time per decode step")
     ap.add_argument("--tokens", type=int, default=4)
     ap.add_argument("--route", choices=["uniform", "zipf"], default="uniform")
     ap.add_argument("--config", choices=["moe", "dense", "prefill"], default="moe",
@@ -227,6 +230,8 @@ class MoeWorkload:
         for li in range(args.layers):
             seed = 1000 + li
             kbits = synth.expert_bits(self.E, seed)
+            if args.stack and li % 8 == 7:
+                kbits = [2] * self.E        # config 4: K = 2 for 1 in 8 layers
             L = synth.make_moe_layer(self.E, self.H, self.I_full, kbits, seed, device=dev, cb=synth.CB_MCG,
                                      rank=rank, world=self.shards)
             if args.route == "zipf":
@@ -346,7 +351,10 @@ class MoeWorkload:
 
     def describe(self):
         a = self.args
-        return {"workload": "config2_moe_decode_layer" if a.route == "uniform" else "config3_moe_decode_layer_zipf",
+        name = "config2_moe_decode_layer" if a.route == "uniform" else "config3_moe_decode_layer_zipf"
+        if a.stack:
+            name = f"config4a_moe_decode_stack_{a.layers}_layers"
+        return {"workload": name,
                 "tokens": a.tokens, "topk": 8, "experts": a.experts, "hidden": 4096, "intermediate": 2048,
                 "intermediate_per_gpu": self.I, "route": a.route, "layers_cycled": a.layers,
                 "unique_experts_per_layer": self.uniq,
@@ -848,6 +856,12 @@ def main():
         "e2e": e2e,
         "clocks": clock_info,
     }
+    if args.config == "moe" and args.stack:
+        # every layer of the stack is cycled through the timed steps; one
+        # decode step runs all of them once
+        step_us = ms_max / K * 1e3 * args.layers
+        line["stack"] = {"layers": args.layers, "us_per_decode_step": step_us,
+                         "tokens_per_s": args.tokens / (step_us / 1e6)}
     if args.config == "moe" and hasattr(wl, "weights_by_k"):
         try:
             line["roofline"]["decode_roof"] = decode_roof(wl.weights_by_k(), kern_avg_ms * 1e3, dev)
