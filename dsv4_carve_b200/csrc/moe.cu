@@ -112,17 +112,26 @@ static __device__ unsigned long long g_phase[PH_N];
 #define PHASE_COUNT(c) (ph_[c] += 1)
 #define PHASE_FLUSH(lane) do { ph_[PH_TOTAL] = clock64() - ph_start_; if ((lane) == 0) for (int i_ = 0; i_ < PH_N; ++i_) atomicAdd(&g_phase[i_], ph_[i_]); } while (0)
 #define PH_ARG , ph_[PH_DATA]
-// Per-CTA timeline (%globaltimer ns): entry, plan built, consumer warp 0 done
-// with its input items, consumer warp 0 / producer / epilogue leave their
-// loops, retire barrier passed, exit.
-static __device__ unsigned long long g_tl[320][8];
-#define TL_MARK(i) do { if ((threadIdx.x & 31) == 0) g_tl[blockIdx.x][i] = globaltimer_ns(); } while (0)
 #else
 #define PHASE_DECL
 #define PHASE_MARK(c)
 #define PHASE_COUNT(c)
 #define PHASE_FLUSH(lane)
 #define PH_ARG
+#endif
+
+// Per-CTA timeline (%globaltimer ns; -DEXL3_TIMELINE, or with the phase
+// clocks): entry, plan built, consumer warp 0 done with its input items,
+// consumer warp 0 / producer / epilogue leave their loops, retire barrier
+// passed, exit.  Eight stores per CTA, so the timing it shows is the plain
+// build's.  Read with exl3_timeline_read.
+#if defined(EXL3_PHASE_CLOCK) && !defined(EXL3_TIMELINE)
+#define EXL3_TIMELINE
+#endif
+#ifdef EXL3_TIMELINE
+static __device__ unsigned long long g_tl[320][8];
+#define TL_MARK(i) do { if ((threadIdx.x & 31) == 0) g_tl[blockIdx.x][i] = globaltimer_ns(); } while (0)
+#else
 #define TL_MARK(i)
 #endif
 
@@ -1093,6 +1102,9 @@ extern "C" int exl3_phase_clock_read(unsigned long long* out, int n, int reset) 
     return EXL3_OK;
 }
 
+#endif
+
+#ifdef EXL3_TIMELINE
 extern "C" int exl3_timeline_read(unsigned long long* out, int n) {
     EXL3_REQUIRE(out && n >= 1 && n <= 320 * 8, EXL3_ERR_ARG, "timeline: bad output");
     EXL3_CUDA(cudaDeviceSynchronize());
