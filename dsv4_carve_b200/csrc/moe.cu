@@ -41,6 +41,7 @@
 
 #include "host.hpp"
 #include "stage.cuh"
+#include "tcgen05.cuh"
 
 namespace exl3 {
 
@@ -540,14 +541,22 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
     uint32_t* cntG = p.ctrl + kOffCntG;
 
     if (tid == 0) TL_MARK(0);
+    // Programmatic dependent launch: the next layer's launch may take SMs as
+    // this grid's CTAs retire.  Up to griddepcontrol.wait this CTA touches only
+    // shared memory and its own inputs (ids), never the scratch, the exchange
+    // buffers or the output that the previous launch in the stream may still use.
+    pdl_launch_dependents();
     if (tid == 0) {
-        S.tp_epoch = p.tp_world > 0 ? __ldcg(reinterpret_cast<const uint32_t*>(p.tp_bufs[p.tp_rank])) + 1u : 0u;
         for (int s = 0; s < p.ring.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kMoeConsumerWarps); }
         for (int s = 0; s < kMoeDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], kMoeConsumerWarps + 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&S.pfull[s], kMoeConsumerWarps); mbar_init(&S.pempty[s], 1); }
         fence_barrier_init();
     }
     build_plan(S.plan, p, tid);     // ends with __syncthreads (also publishes the barrier init)
+    pdl_wait();
+    if (tid == 0)
+        S.tp_epoch = p.tp_world > 0 ? __ldcg(reinterpret_cast<const uint32_t*>(p.tp_bufs[p.tp_rank])) + 1u : 0u;
+    __syncthreads();
     if (tid == 0) TL_MARK(1);
     const MoePlan& P = S.plan;
     const int G = P.G;
@@ -1203,20 +1212,21 @@ int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_
 
     const int smem = kMoeHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * (int) m * kCols * 4;
     auto s = static_cast<cudaStream_t>(stream);
-    if (precise) {
-        switch (cb) {
-            case 0: moe_kernel<0, true><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
-            case 1: moe_kernel<1, true><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
-            default: moe_kernel<2, true><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
-        }
-    } else {
-        switch (cb) {
-            case 0: moe_kernel<0, false><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
-            case 1: moe_kernel<1, false><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
-            default: moe_kernel<2, false><<<pr.grid, kMoeThreads, smem, s>>>(p); break;
-        }
-    }
-    EXL3_CUDA(cudaGetLastError());
+    void (*kern)(MoeParams) = nullptr;
+    if (precise) kern = cb == 0 ? moe_kernel<0, true> : (cb == 1 ? moe_kernel<1, true> : moe_kernel<2, true>);
+    else kern = cb == 0 ? moe_kernel<0, false> : (cb == 1 ? moe_kernel<1, false> : moe_kernel<2, false>);
+    // programmatic stream serialization: see the kernel's prologue
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned) pr.grid);
+    cfg.blockDim = dim3((unsigned) kMoeThreads);
+    cfg.dynamicSmemBytes = (size_t) smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    EXL3_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
     return EXL3_OK;
 }
 
