@@ -8,8 +8,8 @@ TEST INFRASTRUCTURE ONLY.  Produces
   oracle/_ref/vllm_exl3_c_ref*.so      the reference's recipe-lna/lna2/bindings.cpp
                                        built CPU-only as a torch extension
                                        (dequant_cpu + at::mm: the timed CPU baseline)
-The two _ref builds need the reference tree (REF_ROOT, default /root/reference)
-and are skipped when it is absent; the built files travel with the repository
+The two _ref builds need the reference tree (the REF_ROOT environment variable
+names it) and are skipped when it is absent; the built files travel with the repository
 snapshot, so nothing reads the reference tree at run time.
 """
 from __future__ import annotations

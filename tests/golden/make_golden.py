@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
-Run in a container that has the reference tree (REF_ROOT, default
-/root/reference): it builds the reference's own CPU code from source into
+Run in a container that has the reference tree (the REF_ROOT environment
+variable names it): it builds the reference's own CPU code from source into
 oracle/_ref/ (oracle/build_oracle.py: recipe-lna/lna2/bindings.cpp with
 orders/F1-ref/exl3_dequant.cuh) and records what that code returns on seeded
 inputs.  The tests read only the .npz files written here, so they pin the
