@@ -128,7 +128,13 @@ int exl3_linear_group(const void* x, int x_dtype, int64_t rows, int64_t k, int n
  *     ids int32 [m, topk]; weights fp32 [m, topk] (routing scale included).
  * `scratch`: >= exl3_moe_scratch_bytes(m, topk, hidden, inter) bytes, first
  * EXL3_MOE_CTRL_BYTES zero before first use (the kernel restores them).  One
- * launch at a time per scratch buffer. */
+ * launch at a time per scratch buffer.  The kernel is launched with
+ * programmatic stream serialization: it may start while the previous kernel in
+ * the stream is still retiring, reads only `ids` before waiting for that kernel
+ * (griddepcontrol.wait), and waits before everything else.  A preceding kernel
+ * that itself signals griddepcontrol.launch_dependents early must therefore
+ * have written `ids` before it signals (kernels that never signal are waited
+ * for in full, as without the attribute). */
 #define EXL3_MOE_CTRL_BYTES 262144
 int64_t exl3_moe_scratch_bytes(int64_t m, int64_t topk, int64_t hidden, int64_t inter);
 /* Replaces lna2_moe_max_rows (recipe-lna/lna2/lna_moe_ticket.cu:491-492). */
