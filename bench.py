@@ -274,33 +274,77 @@ class MoeWorkload:
                     torch.distributed.barrier()
                     ex.close()
                 self.allreduce_note = self.allreduce_note or "fused exchange setup failed on a peer rank; NCCL used"
-        self._argv = []
-        for li, L in enumerate(self.layers):
+        self._argv = [self.argv_for(li, self.xs[li].data_ptr(), self.routes[li][0].data_ptr(),
+                                    self.routes[li][1].data_ptr(), self.outs[li].data_ptr(), int(args.precise))
+                      for li in range(len(self.layers))]
+        # End-to-end path: each step's inputs (x fp16, ids int32, weights fp32)
+        # sit packed in one pinned host buffer and cross in ONE host-to-device
+        # copy into a device staging buffer, the layer runs through the
+        # pre-bound C-ABI call on views of it, and the output comes back.
+        nx, ni = self.T * self.H * 2, self.T * self.topk * 4
+        self.stage_bytes = nx + 2 * ni
+        self.h_stage, self.d_stage, self.e2e_argv = [], [], []
+        for li in range(len(self.layers)):
             ids, w = self.routes[li]
-            argv = (self.xs[li].data_ptr(), _lib.DT_F16, self.outs[li].data_ptr(), _lib.DT_F16, self.T,
-                    self.H, self.I, *[t.data_ptr() for t in L.table_list()], self.E, L.ktab.data_ptr(),
-                    self.kmax, self.kmax, synth.CB_MCG, ids.data_ptr(), w.data_ptr(), self.topk,
-                    10.0, self.scratch.data_ptr(), self.scratch.numel(), int(args.precise))
-            if self.exchange is not None:
-                argv = argv + (self.exchange.table.data_ptr(), self.exchange.rank, self.exchange.world,
-                               self.exchange.max_rows)
-            self._argv.append(argv)
-        # pinned host copies for the end-to-end path
-        self.h_x = [x.cpu().pin_memory() for x in self.xs]
-        self.h_ids = [r[0].cpu().pin_memory() for r in self.routes]
-        self.h_w = [r[1].cpu().pin_memory() for r in self.routes]
+            h = torch.empty(self.stage_bytes, dtype=torch.uint8).pin_memory()
+            h[:nx].copy_(self.xs[li].cpu().view(torch.uint8).reshape(-1))
+            h[nx:nx + ni].copy_(ids.cpu().view(torch.uint8).reshape(-1))
+            h[nx + ni:].copy_(w.cpu().view(torch.uint8).reshape(-1))
+            d = torch.empty(self.stage_bytes, dtype=torch.uint8, device=dev)
+            base = d.data_ptr()
+            self.h_stage.append(h)
+            self.d_stage.append(d)
+            self.e2e_argv.append(self.argv_for(li, base, base + nx, base + nx + ni, self.outs[li].data_ptr(),
+                                               int(args.precise)))
         self.h_out = [torch.empty((self.T, self.H), dtype=torch.float16).pin_memory() for _ in self.layers]
-        self.d_x = [torch.empty_like(x) for x in self.xs]
-        self.d_ids = [torch.empty_like(r[0]) for r in self.routes]
-        self.d_w = [torch.empty_like(r[1]) for r in self.routes]
-        self.h2d = self.xs[0].numel() * 2 + self.routes[0][0].numel() * 4 + self.routes[0][1].numel() * 4
+        self.h2d = self.stage_bytes
         self.d2h = self.T * self.H * 2
 
-    def launch(self, i, stream_handle):
+    def argv_for(self, li, x_ptr, ids_ptr, w_ptr, out_ptr, precise):
+        """Arguments of exl3_moe_decode (+ the exchange of exl3_moe_decode_tp) for layer li."""
+        from dsv4_carve_b200 import _lib
+
+        L = self.layers[li]
+        argv = (x_ptr, _lib.DT_F16, out_ptr, _lib.DT_F16, self.T, self.H, self.I,
+                *[t.data_ptr() for t in L.table_list()], self.E, L.ktab.data_ptr(), self.kmax, self.kmax,
+                self.synth.CB_MCG, ids_ptr, w_ptr, self.topk, 10.0, self.scratch.data_ptr(), self.scratch.numel(),
+                precise)
+        if self.exchange is not None:
+            argv = argv + (self.exchange.table.data_ptr(), self.exchange.rank, self.exchange.world,
+                           self.exchange.max_rows)
+        return argv
+
+    def call(self, argv, stream_handle):
         fn = self._lib.exl3_moe_decode_tp if self.exchange is not None else self._lib.exl3_moe_decode
-        rc = fn(*self._argv[i % len(self.layers)], stream_handle)
+        rc = fn(*argv, stream_handle)
         if rc:
             raise RuntimeError(self._lib.exl3_last_error().decode())
+
+    def launch(self, i, stream_handle):
+        self.call(self._argv[i % len(self.layers)], stream_handle)
+
+    def check(self, li, snap, stream_handle):
+        """Validation of the timed run (every rank, same collective steps):
+        the device status word; a fresh run of layer li must equal the output
+        the timed region left (`snap`) bit for bit; and the precise arithmetic
+        (fp16-rounded weights, a second computation) must agree with it within
+        2e-3 (times the output scale when that is above 1)."""
+        torch = self.torch
+        dev = self.dev
+        again = torch.empty_like(self.outs[li])
+        prec = torch.empty_like(self.outs[li])
+        ids, w = self.routes[li]
+        self.call(self.argv_for(li, self.xs[li].data_ptr(), ids.data_ptr(), w.data_ptr(), again.data_ptr(),
+                                int(self.args.precise)), stream_handle)
+        self.allreduce(again)
+        self.call(self.argv_for(li, self.xs[li].data_ptr(), ids.data_ptr(), w.data_ptr(), prec.data_ptr(), 1),
+                  stream_handle)
+        self.allreduce(prec)
+        torch.cuda.synchronize(dev)
+        status = self.ext.lna2_moe_status(self.scratch)
+        err = float((snap.float() - prec.float()).abs().max().item())
+        scale = max(1.0, float(prec.float().abs().max().item()))
+        return status, bool(torch.equal(again, snap)), err, 2e-3 * scale
 
     def allreduce(self, out):
         # the fused path has summed over the ranks inside the kernel
@@ -318,19 +362,15 @@ class MoeWorkload:
         self.launch(i, stream_handle)
         self.allreduce(self.outs[i % len(self.layers)])
 
-    def e2e_step(self, i):
-        torch, ext = self.torch, self.ext
+    def e2e_step(self, i, stream_handle):
         li = i % len(self.layers)
-        L = self.layers[li]
-        self.d_x[li].copy_(self.h_x[li], non_blocking=True)
-        self.d_ids[li].copy_(self.h_ids[li], non_blocking=True)
-        self.d_w[li].copy_(self.h_w[li], non_blocking=True)
+        self.d_stage[li].copy_(self.h_stage[li], non_blocking=True)
         out = self.outs[li]
-        ext.lna2_moe_decode(self.d_x[li], out, *L.table_list(), self.d_ids[li], self.d_w[li], self.kmax, 10.0,
-                            self.scratch, intermediate=self.I, k_table=L.ktab, codebook=L.cb,
-                            precise=self.args.precise, tp_exchange=self.exchange)
+        self.call(self.e2e_argv[li], stream_handle)
         self.allreduce(out)
         self.h_out[li].copy_(out, non_blocking=True)
+
+    e2e_api = "C ABI exl3_moe_decode (exl3_moe_decode_tp for N > 1), inputs in one pinned staging buffer"
 
     def bytes_per_step(self, i):
         return self.ubytes[i % len(self.layers)]
@@ -437,7 +477,37 @@ class PrefillWorkload:
         self.launch(i, stream_handle)
         self.allreduce(self.outs[i % len(self.layers)])
 
-    def e2e_step(self, i):
+    def check(self, li, snap, stream_handle):
+        """Status word; a fresh run equals the timed region's output bit for
+        bit; the decode kernel (precise arithmetic, the same fp16-rounded
+        weights) on the chunk's first 32 tokens agrees within 2e-3."""
+        torch = self.torch
+        again = torch.empty_like(self.outs[li])
+        a = list(self._argv[li])
+        a[2] = again.data_ptr()
+        rc = self.lib.exl3_moe_prefill(*a, stream_handle)
+        if rc:
+            raise RuntimeError(self.lib.exl3_last_error().decode())
+        self.allreduce(again)
+        L = self.layers[li]
+        ids, w = self.routes[li]
+        n = min(32, self.T)
+        dec = torch.empty((n, self.H), dtype=torch.bfloat16, device=self.dev)
+        dscr = torch.zeros(self.ext.lna2_moe_scratch_bytes(n, self.topk, self.H, self.I), dtype=torch.uint8,
+                           device=self.dev)
+        self.ext.lna2_moe_decode(self.xs[li][:n].contiguous(), dec, *L.table_list(), ids[:n].contiguous(),
+                                 w[:n].contiguous(), 3, 10.0, dscr, intermediate=self.I, k_table=L.ktab,
+                                 codebook=L.cb, precise=True)
+        self.allreduce(dec)
+        torch.cuda.synchronize(self.dev)
+        status = self.ext.lna2_moe_status(self.scratch) | self.ext.lna2_moe_status(dscr)
+        err = float((snap[:n].float() - dec.float()).abs().max().item())
+        scale = max(1.0, float(dec.float().abs().max().item()))
+        return status, bool(torch.equal(again, snap)), err, 2e-3 * scale
+
+    e2e_api = "vllm_exl3_c.lna2_moe_prefill"
+
+    def e2e_step(self, i, stream_handle):
         li = i % len(self.layers)
         L = self.layers[li]
         x = self.xs[li]
@@ -565,7 +635,31 @@ class DenseWorkload:
         self.launch(i, stream_handle)
         self.allreduce(self.outs[i % len(self.sets)])
 
-    def e2e_step(self, i):
+    def check(self, li, snap, stream_handle):
+        """Status word of the linear scratch; a fresh run of set li equals the
+        timed region's output bit for bit; the fast arithmetic (unrounded
+        weights, a second computation) agrees within 2e-3."""
+        torch = self.torch
+        a, b, c = self.sets[li]
+        xin = self.xs[li][2]
+        again = self.ext.linear_forward(xin, c.trellis, c.suh, c.svh, 6, 0, torch.float16, True)
+        fast = self.ext.linear_forward(xin, c.trellis, c.suh, c.svh, 6, 0, torch.float16, False)
+        self.allreduce(again)
+        self.allreduce(fast)
+        torch.cuda.synchronize(self.dev)
+        import ctypes
+
+        word = ctypes.c_uint32(0)
+        from dsv4_carve_b200 import _lib
+
+        _lib.check(self.lib.exl3_scratch_status(self.scratch.data_ptr(), 0, 0, ctypes.addressof(word), stream_handle))
+        err = float((snap.float() - fast.float()).abs().max().item())
+        scale = max(1.0, float(fast.float().abs().max().item()))
+        return int(word.value), bool(torch.equal(again, snap)), err, 2e-3 * scale
+
+    e2e_api = "vllm_exl3_c.linear_forward"
+
+    def e2e_step(self, i, stream_handle):
         """x from pinned host memory, the three linears through the public
         linear_forward call, the last output back to pinned host memory."""
         torch = self.torch
@@ -781,6 +875,9 @@ def main():
     barrier()
     t_wall1 = time.time()
     ms = start.elapsed_time(end)
+    # the last layer the timed region ran, and the output it left, for the check
+    last_li = (K - 1) % len(wl.layers)
+    snap = wl.outs[last_li].clone()
     # per-launch kernel durations (roofline.achieved): a second pass with
     # events around each launch
     for i in range(K):
@@ -806,14 +903,14 @@ def main():
     e2e = None
     if not args.no_e2e:
         for i in range(min(3, args.warmup) or 1):
-            wl.e2e_step(i)
+            wl.e2e_step(i, sh)
         torch.cuda.synchronize(dev)
         barrier()
         torch.cuda.synchronize(dev)
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record(stream)
         for i in range(K):
-            wl.e2e_step(i)
+            wl.e2e_step(i, sh)
         e2.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
@@ -822,9 +919,20 @@ def main():
             torch.distributed.all_reduce(ms2, op=torch.distributed.ReduceOp.MAX)
         e2e = {"value": all_bytes / (float(ms2.item()) / 1e3) / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
-               "ms_per_step": float(ms2.item()) / K,
-               "api": {"dense": "vllm_exl3_c.linear_forward", "prefill": "vllm_exl3_c.lna2_moe_prefill"}.get(
-                   args.config, "vllm_exl3_c.lna2_moe_decode")}
+               "ms_per_step": float(ms2.item()) / K, "api": wl.e2e_api}
+
+    # ---- validation: status words and a second computation of one layer
+    status, same, err, tol = wl.check(last_li, snap, sh)
+    chk = torch.tensor([float(status), 0.0 if same else 1.0, err / tol], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(chk, op=torch.distributed.ReduceOp.MAX)
+    status_all, differs, err_ratio = int(chk[0].item()), bool(chk[1].item()), float(chk[2].item())
+    check = {"status_word": status_all, "rerun_bitwise_equal": not differs,
+             "second_computation_max_abs_over_tol": err_ratio,
+             "ok": status_all == 0 and not differs and err_ratio <= 1.0,
+             "how": ("device status word of every rank after the timed and e2e loops; a fresh run of the last "
+                     "timed layer must equal the output the timed region left bit for bit; a second "
+                     "computation in the other arithmetic must agree within 2e-3 (max over ranks)")}
 
     clock_info = None
     if clocks:
@@ -860,10 +968,16 @@ def main():
         "config": wl.describe(),
         "roofline": {"bound": "hbm", "kernel": wl.kernel_name, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
-                     "kernel_us_avg": kern_avg_ms * 1e3},
+                     "traffic": traffic,
+                     "traffic_source": ("ncu capture in profiles/, scaled from the captured launch's algorithmic "
+                                        "bytes to this run's" if traffic is not None else None),
+                     "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "kernel_us_avg": kern_avg_ms * 1e3,
+                     "kernel_us_source": ("second, serialised pass with CUDA events around each launch (the events "
+                                          "stop the launch overlap, so this is slower than ms_per_step)")},
         "gpu_launches": K * wl.launches_per_step,
         "e2e": e2e,
+        "check": check,
         "clocks": clock_info,
     }
     if args.config == "moe" and args.stack:
@@ -884,6 +998,8 @@ def main():
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+    if not check["ok"]:
+        sys.exit("bench: the validation check failed (see the line's `check`); the numbers are not valid")
 
 
 if __name__ == "__main__":

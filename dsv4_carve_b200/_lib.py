@@ -48,6 +48,10 @@ _SIGS = {
     "exl3_tp_ipc_close": (_I, [_P]),
     "exl3_moe_decode_tp": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
                            + [_I64, _P, _I, _I, _I, _P, _P, _I64, C.c_float, _P, _I64, _I, _P, _I, _I, _I64, _P]),
+    "exl3_moe_decode_routed": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
+                               + [_I64, _P, _I, _I, _I, _P, _I64, C.c_float, _P, _I64, _I, _P, _I, _I, _I64, _P]),
+    "exl3_moe_prefill_routed": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
+                                + [_I64, _P, _I, _I, _I, _P, _I64, C.c_float, _P, _I64, _P]),
     "exl3_moe_prefill_scratch_bytes": (_I64, [_I64, _I64, _I64, _I64, _I64]),
     "exl3_moe_prefill_chunk_tokens": (_I64, [_I64]),
     "exl3_moe_prefill": (_I, [_P, _I, _P, _I, _I64, _I64, _I64] + [_P] * 9
@@ -58,6 +62,13 @@ _SIGS = {
     "exl3_decode_roof_out_floats": (_I64, []),
     "exl3_decode_roof": (_I, [_I, _I, _I, _P, _I64, _P, _I64, _P, _P]),
 }
+
+
+class MoeRoute(C.Structure):
+    """exl3_moe_route of include/exl3_b200.h."""
+    _fields_ = [("ids", C.c_void_p), ("ids_dtype", C.c_int), ("weights", C.c_void_p), ("weights_dtype", C.c_int),
+                ("expert_map", C.c_void_p), ("n_global", C.c_int64)]
+
 
 _lib = None
 

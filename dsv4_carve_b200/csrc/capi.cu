@@ -34,7 +34,7 @@ int device_info(int device, DeviceInfo* out) {
 
 }  // namespace exl3
 
-extern "C" int exl3_abi_version(void) { return 1; }
+extern "C" int exl3_abi_version(void) { return 2; }
 
 extern "C" const char* exl3_last_error(void) { return exl3::g_last_error; }
 

@@ -227,4 +227,37 @@ __device__ __forceinline__ void store_out(void* out, int dtype, int64_t i, float
     else reinterpret_cast<float*>(out)[i] = v;
 }
 
+// ---------------------------------------------------------------- routes
+// Router outputs as the serving layer holds them: expert ids int32 or int64
+// [m, topk], global ids when an expert map is given; routing weights fp32,
+// bf16 or fp16.  The reference casts and maps them with torch before its
+// kernel (recipe-lna/vllm_exl3_exl3.py.lna:963-987,1234-1236); here every
+// read goes through these helpers instead.
+struct RouteIn {
+    const void* ids;
+    const void* weights;
+    const int64_t* emap;      // global id -> local id (< 0: not on this rank), or null
+    int64_t n_global;         // entries of emap
+    int ids64;                // 0: int32 ids, 1: int64 ids
+    int w_dtype;              // 0 fp16, 1 bf16, 2 fp32
+};
+
+// Local expert of slot s, or -1 when the slot is skipped: a negative id, an
+// id past the map, an id the map sends off this rank (negative), or a local
+// id outside [0, E) -- the cases the reference maps to its n_local sentinel.
+__device__ __forceinline__ int route_local_id(const RouteIn& r, int64_t s, int E) {
+    int64_t v = r.ids64 ? reinterpret_cast<const int64_t*>(r.ids)[s] : (int64_t) reinterpret_cast<const int32_t*>(r.ids)[s];
+    if (r.emap != nullptr) {
+        if (v < 0 || v >= r.n_global) return -1;
+        v = r.emap[v];
+    }
+    return (v >= 0 && v < (int64_t) E) ? (int) v : -1;
+}
+
+__device__ __forceinline__ float route_weight(const RouteIn& r, int64_t s) {
+    if (r.w_dtype == 2) return reinterpret_cast<const float*>(r.weights)[s];
+    if (r.w_dtype == 1) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(r.weights)[s]);
+    return __half2float(reinterpret_cast<const __half*>(r.weights)[s]);
+}
+
 }  // namespace exl3

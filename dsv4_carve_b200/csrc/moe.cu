@@ -154,8 +154,7 @@ struct MoeParams {
     void* out;
     const int64_t* tab[9];      // gate t/su/sv, up t/su/sv, down t/su/sv
     const int32_t* ktab;        // per-expert K, or null (then kuni)
-    const int32_t* ids;
-    const float* weights;
+    RouteIn route;              // expert ids / routing weights (dtype, optional expert map)
     int x_dtype, out_dtype;
     int m, H, I, topk, E, kuni;
     float limit;
@@ -198,8 +197,8 @@ __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
     __syncthreads();
     const int nslots = p.m * p.topk;
     for (int s = tid; s < nslots; s += nthr) {
-        const int id = p.ids[s];
-        if (id >= 0 && id < p.E) atomicOr(&P.emask[id], 1u << (s / p.topk));
+        const int id = route_local_id(p.route, s, p.E);
+        if (id >= 0) atomicOr(&P.emask[id], 1u << (s / p.topk));
     }
     __syncthreads();
     // Each worker thread owns experts [4t, 4t+4) (E <= 1024).
@@ -248,9 +247,9 @@ __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
     }
     __syncthreads();
     for (int s = tid; s < nslots; s += nthr) {
-        const int id = p.ids[s];
+        const int id = route_local_id(p.route, s, p.E);
         short sp = -1;
-        if (id >= 0 && id < p.E) {
+        if (id >= 0) {
             const int row = s / p.topk;
             sp = (short) (P.epair[id] + __popc(P.emask[id] & ((1u << row) - 1u)));
         }
@@ -504,7 +503,7 @@ __device__ void moe_finish_b_count(const MoeParams& p, const MoePlan& P, int blk
                 const int k = k0 + j;
                 const int pr = k < p.topk ? (int) P.slotpair[r * p.topk + k] : -1;
                 ok[j] = pr >= 0;
-                wv[j] = ok[j] ? p.weights[r * p.topk + k] : 0.f;
+                wv[j] = ok[j] ? route_weight(p.route, r * p.topk + k) : 0.f;
                 d[j] = __ldcg(reinterpret_cast<const float4*>(p.downc + (int64_t) (ok[j] ? pr : 0) * p.H +
                                                                blk * kCols + lane * 4));
             }
@@ -1135,10 +1134,14 @@ int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_
                     const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
                     const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
                     const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh, int64_t n_experts,
-                    const int32_t* k_table, int K, int kmax, int cb, const int32_t* ids, const float* weights,
-                    int64_t topk, float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise,
-                    const TpArgs& tp, void* stream) {
-    EXL3_REQUIRE(x && out && ids && weights && scratch, EXL3_ERR_ARG, "moe: null pointer argument");
+                    const int32_t* k_table, int K, int kmax, int cb, const RouteIn& route, int64_t topk,
+                    float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise, const TpArgs& tp,
+                    void* stream) {
+    EXL3_REQUIRE(x && out && route.ids && route.weights && scratch, EXL3_ERR_ARG, "moe: null pointer argument");
+    EXL3_REQUIRE(route.ids64 == 0 || route.ids64 == 1, EXL3_ERR_ARG, "moe: ids dtype must be 0 (int32) or 1 (int64)");
+    EXL3_REQUIRE(route.w_dtype >= 0 && route.w_dtype <= 2, EXL3_ERR_ARG, "moe: routing weight dtype code out of range");
+    EXL3_REQUIRE(route.emap == nullptr || (route.n_global >= 1 && route.n_global <= (int64_t) 1 << 31), EXL3_ERR_ARG,
+                 "moe: expert map must have 1..2^31 entries");
     const int64_t* tabs[9] = {gate_trellis, gate_suh, gate_svh, up_trellis, up_suh,
                               up_svh,       down_trellis, down_suh, down_svh};
     for (int i = 0; i < 9; ++i) EXL3_REQUIRE(tabs[i], EXL3_ERR_ARG, "moe: null pointer table %d", i);
@@ -1175,8 +1178,7 @@ int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_
     for (int i = 0; i < 9; ++i) p.tab[i] = tabs[i];
     p.ktab = k_table;
     p.kuni = K;
-    p.ids = ids;
-    p.weights = weights;
+    p.route = route;
     p.x_dtype = x_dtype;
     p.out_dtype = out_dtype;
     p.m = (int) m;
@@ -1240,10 +1242,55 @@ extern "C" int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dt
                                const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
                                int cb, const int32_t* ids, const float* weights, int64_t topk, float swiglu_limit,
                                void* scratch, int64_t scratch_bytes, int precise, void* stream) {
+    const exl3::RouteIn route{ids, weights, nullptr, 0, 0, 2};
     return exl3::moe_decode_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
                                  up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K,
-                                 kmax, cb, ids, weights, topk, swiglu_limit, scratch, scratch_bytes, precise,
+                                 kmax, cb, route, topk, swiglu_limit, scratch, scratch_bytes, precise,
                                  exl3::TpArgs{}, stream);
+}
+
+namespace exl3 {
+// The C-ABI route descriptor as the kernels' RouteIn (an error code when it is invalid).
+int route_from_abi(const exl3_moe_route* r, RouteIn* out) {
+    EXL3_REQUIRE(r != nullptr, EXL3_ERR_ARG, "moe: null route descriptor");
+    EXL3_REQUIRE(r->ids_dtype == 0 || r->ids_dtype == 1, EXL3_ERR_ARG,
+                 "moe: route ids_dtype must be 0 (int32) or 1 (int64)");
+    EXL3_REQUIRE(r->weights_dtype >= EXL3_DTYPE_F16 && r->weights_dtype <= EXL3_DTYPE_F32, EXL3_ERR_ARG,
+                 "moe: route weights_dtype must be fp16, bf16 or fp32");
+    EXL3_REQUIRE(r->expert_map == nullptr || r->n_global >= 1, EXL3_ERR_ARG,
+                 "moe: route expert_map given with n_global < 1");
+    *out = RouteIn{r->ids, r->weights, r->expert_map, r->expert_map ? r->n_global : 0, r->ids_dtype,
+                   r->weights_dtype};
+    return EXL3_OK;
+}
+}  // namespace exl3
+
+extern "C" int exl3_moe_decode_routed(const void* x, int x_dtype, void* out, int out_dtype, int64_t m,
+                                      int64_t hidden, int64_t inter, const int64_t* gate_trellis,
+                                      const int64_t* gate_suh, const int64_t* gate_svh, const int64_t* up_trellis,
+                                      const int64_t* up_suh, const int64_t* up_svh, const int64_t* down_trellis,
+                                      const int64_t* down_suh, const int64_t* down_svh, int64_t n_experts,
+                                      const int32_t* k_table, int K, int kmax, int cb, const exl3_moe_route* route,
+                                      int64_t topk, float swiglu_limit, void* scratch, int64_t scratch_bytes,
+                                      int precise, const int64_t* tp_bufs, int tp_rank, int tp_world,
+                                      int64_t tp_max_rows, void* stream) {
+    exl3::RouteIn r;
+    if (int rc = exl3::route_from_abi(route, &r)) return rc;
+    exl3::TpArgs tp;
+    if (tp_bufs != nullptr) {
+        EXL3_REQUIRE(tp_world >= 1 && tp_world <= 32 && tp_rank >= 0 && tp_rank < tp_world, EXL3_ERR_ARG,
+                     "moe tp: rank %d of world %d out of range (world 1..32)", tp_rank, tp_world);
+        EXL3_REQUIRE(m <= tp_max_rows && tp_max_rows <= exl3::kMoeMaxRows, EXL3_ERR_ARG,
+                     "moe tp: m = %lld above the exchange buffers' row capacity %lld", (long long) m,
+                     (long long) tp_max_rows);
+        tp.bufs = tp_bufs;
+        tp.rank = tp_rank;
+        tp.world = tp_world;
+        tp.mcap = tp_max_rows;
+    }
+    return exl3::moe_decode_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
+                                 up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K,
+                                 kmax, cb, r, topk, swiglu_limit, scratch, scratch_bytes, precise, tp, stream);
 }
 
 // ------------------------------------------------------------------ fused tensor-parallel sum
@@ -1316,23 +1363,22 @@ extern "C" int exl3_moe_decode_tp(const void* x, int x_dtype, void* out, int out
     tp.rank = tp_rank;
     tp.world = tp_world;
     tp.mcap = tp_max_rows;
+    const exl3::RouteIn route{ids, weights, nullptr, 0, 0, 2};
     return exl3::moe_decode_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
                                  up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K,
-                                 kmax, cb, ids, weights, topk, swiglu_limit, scratch, scratch_bytes, precise, tp,
-                                 stream);
+                                 kmax, cb, route, topk, swiglu_limit, scratch, scratch_bytes, precise, tp, stream);
 }
 
 // ------------------------------------------------------------------ allocation-free variant
 // exl3_moe_decode_noalloc: the same layer as exl3_moe_decode for callers that
-// may not allocate device memory at all -- code running while a CUDA graph is
-// being captured (an allocation there is either illegal or baked into the
-// graph), hosts whose memory is owned by another allocator and who therefore
-// cannot hand out a scratch buffer, and latency-critical callers that cannot
-// afford cudaMalloc's implicit synchronization.  Its scratch is the array
-// below, compiled into the library: EXL3_MOE_STATIC_SCRATCH_BYTES (8 MiB) of
-// device memory that every GPU which loads the library holds until the
-// process exits.  Geometries whose scratch (exl3_moe_scratch_bytes) exceeds it
-// are rejected.
+// cannot allocate device memory at all -- a plugin inside a serving process
+// whose device memory is owned by the host's caching allocator (no cudaMalloc
+// of its own, and no buffer handed to it), and latency-critical callers that
+// cannot afford cudaMalloc's implicit synchronization.  Its scratch is the
+// array below, compiled into the library: EXL3_MOE_STATIC_SCRATCH_BYTES
+// (8 MiB) of device memory that every GPU which loads the library holds until
+// the process exits.  Geometries whose scratch (exl3_moe_scratch_bytes)
+// exceeds it are rejected.
 namespace exl3 {
 namespace {
 

@@ -225,8 +225,8 @@ __device__ int block_scan_1024(int v, int* warp_tot, int* total) {
 // is the argsort / count glue it replaces).  Pairs are ordered by expert,
 // then token, so results do not depend on timing; an expert listed twice in
 // one token's slots is one pair used by both slots.
-__global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T, int topk, int E, int H, int I,
-                                                       uint32_t* ctrl, PfPlan plan) {
+__global__ void __launch_bounds__(1024) pf_plan_kernel(RouteIn route, int64_t slot0, int T, int topk, int E, int H,
+                                                       int I, uint32_t* ctrl, PfPlan plan) {
     extern __shared__ uint32_t pf_mask[];   // [E][W]
     __shared__ int warp_tot[32];
     __shared__ int totals[4];
@@ -237,8 +237,8 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
     for (int i = tid; i < E * W; i += 1024) pf_mask[i] = 0u;
     __syncthreads();
     for (int q = tid; q < T * topk; q += 1024) {
-        const int e = ids[q], t = q / topk;
-        if (e >= 0 && e < E) atomicOr(&pf_mask[e * W + (t >> 5)], 1u << (t & 31));
+        const int e = route_local_id(route, slot0 + q, E), t = q / topk;
+        if (e >= 0) atomicOr(&pf_mask[e * W + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
     // per expert: pairs, passes, units; E <= 1024 = one expert per thread
@@ -301,9 +301,9 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int32_t* ids, int T
     }
     // slot -> pair
     for (int q = tid; q < T * topk; q += 1024) {
-        const int e = ids[q], t = q / topk;
+        const int e = route_local_id(route, slot0 + q, E), t = q / topk;
         int pr = -1;
-        if (e >= 0 && e < E) {
+        if (e >= 0) {
             const int w = t >> 5;
             pr = s_pair[e] + __popc(pf_mask[e * W + w] & ((1u << (t & 31)) - 1u));
             for (int w2 = 0; w2 < w; ++w2) pr += __popc(pf_mask[e * W + w2]);
@@ -811,8 +811,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
 // ------------------------------------------------------------------ 4. gather
 // out[t][c] = sum over slots j, in slot order, of weights[t][j] * dn[pair][c]
 // (recipe-lna/lna2/lna_moe_ticket.cu:409-428), fp32, one cast.
-__global__ void __launch_bounds__(256) pf_gather_kernel(const float* dn, const int* slot_pair, const float* weights,
-                                                        int T, int topk, int H, void* out, int out_dtype) {
+__global__ void __launch_bounds__(256) pf_gather_kernel(const float* dn, const int* slot_pair, RouteIn route,
+                                                        int64_t slot0, int T, int topk, int H, void* out,
+                                                        int out_dtype) {
     pdl_wait();
     const int64_t n4 = (int64_t) T * (H / 4);
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t) gridDim.x * blockDim.x) {
@@ -822,7 +823,7 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(const float* dn, const i
         for (int j = 0; j < topk; ++j) {
             const int pr = slot_pair[t * topk + j];
             if (pr < 0) continue;
-            const float w = weights[t * topk + j];
+            const float w = route_weight(route, slot0 + t * topk + j);
             const float4 d = __ldcg(reinterpret_cast<const float4*>(dn + (int64_t) pr * H + c));
             v[0] += w * d.x; v[1] += w * d.y; v[2] += w * d.z; v[3] += w * d.w;
         }
@@ -982,14 +983,17 @@ extern "C" int64_t exl3_moe_prefill_chunk_tokens(int64_t n_experts) {
     return pf_chunk_tokens(n_experts);
 }
 
-extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
-                                int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
-                                const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
-                                const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
-                                const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
-                                int cb, const int32_t* ids, const float* weights, int64_t topk, float swiglu_limit,
-                                void* scratch, int64_t scratch_bytes, void* stream) {
-    EXL3_REQUIRE(x && out && ids && weights && scratch, EXL3_ERR_ARG, "exl3_moe_prefill: null pointer argument");
+int route_from_abi(const exl3_moe_route* r, RouteIn* out);   // moe.cu
+
+static int moe_prefill_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
+                            int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
+                            const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
+                            const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
+                            const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
+                            int cb, const RouteIn& route, int64_t topk, float swiglu_limit, void* scratch,
+                            int64_t scratch_bytes, void* stream) {
+    EXL3_REQUIRE(x && out && route.ids && route.weights && scratch, EXL3_ERR_ARG,
+                 "exl3_moe_prefill: null pointer argument");
     EXL3_REQUIRE(gate_trellis && gate_suh && gate_svh && up_trellis && up_suh && up_svh && down_trellis &&
                      down_suh && down_svh,
                  EXL3_ERR_ARG, "exl3_moe_prefill: null pointer table");
@@ -1085,11 +1089,10 @@ extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_d
         const int T = (int) (m - t0 < ct ? m - t0 : ct);
         const void* xc = static_cast<const uint8_t*>(x) + t0 * hidden * xb;
         void* oc = static_cast<uint8_t*>(out) + t0 * hidden * ob;
-        const int32_t* idc = ids + t0 * topk;
-        const float* wc = weights + t0 * topk;
+        const int64_t slot0 = t0 * topk;
         const int W = (T + 31) / 32;
-        EXL3_CUDA(pf_launch(pf_plan_kernel, dim3(1), dim3(1024), (int) (n_experts * W * 4), s, false, idc, T,
-                            (int) topk, (int) n_experts, (int) hidden, (int) inter, p.ctrl, p.plan));
+        EXL3_CUDA(pf_launch(pf_plan_kernel, dim3(1), dim3(1024), (int) (n_experts * W * 4), s, false, route, slot0,
+                            T, (int) topk, (int) n_experts, (int) hidden, (int) inter, p.ctrl, p.plan));
         int64_t ib = (int64_t) T * topk;
         if (ib > (int64_t) di.sms * 8) ib = (int64_t) di.sms * 8;
         EXL3_CUDA(pf_launch(pf_input_kernel, dim3((unsigned) ib), dim3(256), 0, s, true, xc, x_dtype, (int) hidden,
@@ -1104,9 +1107,38 @@ extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_d
         int64_t gb = ((int64_t) T * (hidden / 4) + 255) / 256;
         if (gb > (int64_t) di.sms * 8) gb = (int64_t) di.sms * 8;
         EXL3_CUDA(pf_launch(pf_gather_kernel, dim3((unsigned) gb), dim3(256), 0, s, true, (const float*) p.dn,
-                            (const int*) p.plan.slot_pair, wc, T, (int) topk, (int) hidden, oc, out_dtype));
+                            (const int*) p.plan.slot_pair, route, slot0, T, (int) topk, (int) hidden, oc,
+                            out_dtype));
     }
     return EXL3_OK;
+}
+
+extern "C" int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_dtype, int64_t m, int64_t hidden,
+                                int64_t inter, const int64_t* gate_trellis, const int64_t* gate_suh,
+                                const int64_t* gate_svh, const int64_t* up_trellis, const int64_t* up_suh,
+                                const int64_t* up_svh, const int64_t* down_trellis, const int64_t* down_suh,
+                                const int64_t* down_svh, int64_t n_experts, const int32_t* k_table, int K, int kmax,
+                                int cb, const int32_t* ids, const float* weights, int64_t topk, float swiglu_limit,
+                                void* scratch, int64_t scratch_bytes, void* stream) {
+    const RouteIn route{ids, weights, nullptr, 0, 0, 2};
+    return moe_prefill_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
+                            up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K, kmax,
+                            cb, route, topk, swiglu_limit, scratch, scratch_bytes, stream);
+}
+
+extern "C" int exl3_moe_prefill_routed(const void* x, int x_dtype, void* out, int out_dtype, int64_t m,
+                                       int64_t hidden, int64_t inter, const int64_t* gate_trellis,
+                                       const int64_t* gate_suh, const int64_t* gate_svh, const int64_t* up_trellis,
+                                       const int64_t* up_suh, const int64_t* up_svh, const int64_t* down_trellis,
+                                       const int64_t* down_suh, const int64_t* down_svh, int64_t n_experts,
+                                       const int32_t* k_table, int K, int kmax, int cb, const exl3_moe_route* route,
+                                       int64_t topk, float swiglu_limit, void* scratch, int64_t scratch_bytes,
+                                       void* stream) {
+    RouteIn r;
+    if (int rc = route_from_abi(route, &r)) return rc;
+    return moe_prefill_impl(x, x_dtype, out, out_dtype, m, hidden, inter, gate_trellis, gate_suh, gate_svh,
+                            up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh, n_experts, k_table, K, kmax,
+                            cb, r, topk, swiglu_limit, scratch, scratch_bytes, stream);
 }
 
 }  // namespace exl3

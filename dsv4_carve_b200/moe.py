@@ -1,13 +1,16 @@
 """Plugin-side glue of the routed-MoE decode path.
 
-Restates what the vllm-exl3 plugin does around the native kernel
-(recipe-lna/vllm_exl3_exl3.py.lna): local id mapping (``map_topk_to_local``,
-:963-987), the load-time pointer-table contract (:1318-1374, :1552-1570),
-one shared zeroed scratch per device created before any graph capture
-(:1276-1296), the strict / call-counter / decline instrumentation
-(:1070-1157) and the dispatch itself (``_apply_lna2_moe``, :1190-1248),
-generalised to per-expert bit widths, top-k up to 16 and any 128-multiple
-hidden / intermediate width.
+Covers what the vllm-exl3 plugin does around the native kernel
+(recipe-lna/vllm_exl3_exl3.py.lna): the load-time pointer-table contract
+(:1318-1374, :1552-1570), one shared zeroed scratch per device created
+before any graph capture (:1276-1296), the strict / call-counter / decline
+instrumentation (:1070-1157) and the dispatch itself (``_apply_lna2_moe``,
+:1190-1248), generalised to per-expert bit widths, top-k up to 16 and any
+128-multiple hidden / intermediate width.  The plugin's per-layer torch glue
+-- global-to-local id mapping through ``expert_map`` and the id / weight
+casts (:963-987, :1234-1236) -- is not done here at all: the router's
+outputs go to the kernel as they are and the kernel's route plan maps and
+converts them, so a layer is one launch.
 """
 from __future__ import annotations
 
@@ -59,19 +62,22 @@ def _decline(why: str, *, not_ready: bool = False) -> None:
         raise RuntimeError(f"VLLM_EXL3_MOE_STRICT={level}, but the B200 MoE kernel declined this call: {why}")
 
 
-def map_topk_to_local(ids: torch.Tensor, n_local: int, expert_map: torch.Tensor | None) -> torch.Tensor:
-    """Global expert ids [T, k] -> local ids; invalid or non-local -> n_local sentinel."""
-    flat = ids.reshape(-1)
-    if expert_map is None:
-        invalid = (flat < 0) | (flat >= n_local)
-        return torch.where(invalid, flat.new_full(flat.shape, n_local), flat)
-    if expert_map.device != flat.device or expert_map.dtype != torch.long:
-        raise RuntimeError("EXL3 expert_map is not pinned to the hidden-state device")
-    n_global = int(expert_map.numel())
-    safe = flat.clamp(min=0, max=max(n_global - 1, 0))
-    mapped = expert_map[safe] if n_global else flat.new_full(flat.shape, n_local)
-    invalid = (flat < 0) | (flat >= n_global) | (mapped < 0) | (mapped >= n_local)
-    return torch.where(invalid, flat.new_full(flat.shape, n_local), mapped)
+def _router_outputs(ids: torch.Tensor, weights: torch.Tensor, expert_map: torch.Tensor | None):
+    """ids / weights / map as the kernel reads them; views only, unless a
+    tensor comes in a layout or dtype the kernel does not read."""
+    if ids.dtype not in (torch.int32, torch.int64):
+        ids = ids.to(torch.int64)
+    ids = ids.reshape(ids.shape[0], -1) if ids.dim() != 2 else ids
+    if not ids.is_contiguous():
+        ids = ids.contiguous()
+    w = weights.reshape(ids.shape)
+    if w.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        w = w.to(torch.float32)
+    if not w.is_contiguous():
+        w = w.contiguous()
+    if expert_map is not None and (expert_map.device != ids.device or expert_map.dtype != torch.long):
+        raise RuntimeError("EXL3 expert_map is not pinned to the hidden-state device as int64")
+    return ids, w
 
 
 @dataclass
@@ -185,18 +191,17 @@ def apply_moe_decode(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor
             or int(x2d.shape[1]) != state.hidden or T * int(ids.shape[-1]) > 256 or int(ids.shape[-1]) > 16):
         _decline(f"geometry x={tuple(x2d.shape)} topk={int(ids.shape[-1])}")
         return None
-    local = map_topk_to_local(ids, state.n_experts, expert_map).reshape(ids.shape)
-    safe_ids = local.to(torch.int32).contiguous()
-    route_w = weights.reshape(local.shape).to(torch.float32).contiguous()
-    x = x2d if x2d.dtype in (torch.float16, torch.bfloat16) else x2d.to(torch.float16)
+    ids2, route_w = _router_outputs(ids, weights, expert_map)
+    x = x2d if x2d.dtype in (torch.float16, torch.bfloat16, torch.float32) else x2d.to(torch.float16)
     x = x.contiguous()
     scratch = moe_scratch_for(x.device, _ext.lna2_moe_scratch_bytes(
-        _ext.lna2_moe_max_rows(), max(8, int(ids.shape[-1])), state.hidden, state.inter))
+        _ext.lna2_moe_max_rows(), max(8, int(ids2.shape[-1])), state.hidden, state.inter))
     if out is None:
-        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
-    _ext.lna2_moe_decode(x, out, *state.table_list(), safe_ids, route_w, state.kmax, float(limit), scratch,
-                         intermediate=state.inter, k_table=state.ktab, codebook=state.codebook,
-                         precise=state.precise)
+        out = torch.empty(x.shape, dtype=out_dtype or (x.dtype if x.dtype != torch.float32 else torch.float16),
+                          device=x.device)
+    _ext.lna2_moe_decode_routed(x, out, *state.table_list(), ids2, route_w, state.kmax, float(limit), scratch,
+                                intermediate=state.inter, k_table=state.ktab, codebook=state.codebook,
+                                precise=state.precise, expert_map=expert_map)
     _CALLS["b200"] += 1
     if not _ACTIVE_LOGGED:
         _ACTIVE_LOGGED = True
@@ -217,17 +222,16 @@ def apply_moe_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
             or int(ids.shape[-1]) > 16 or state.kmax > 4):
         _decline(f"prefill geometry x={tuple(x2d.shape)} topk={int(ids.shape[-1])}")
         return None
-    local = map_topk_to_local(ids, state.n_experts, expert_map).reshape(ids.shape)
-    safe_ids = local.to(torch.int32).contiguous()
-    route_w = weights.reshape(local.shape).to(torch.float32).contiguous()
+    ids2, route_w = _router_outputs(ids, weights, expert_map)
     x = x2d if x2d.dtype in (torch.float16, torch.bfloat16) else x2d.to(torch.float16)
     x = x.contiguous()
     scratch = _ext._prefill_scratch(x.device, _ext.lna2_moe_prefill_scratch_bytes(
-        T, int(ids.shape[-1]), state.hidden, state.inter, state.n_experts))
+        T, int(ids2.shape[-1]), state.hidden, state.inter, state.n_experts))
     if out is None:
         out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
-    _ext.lna2_moe_prefill(x, out, *state.table_list(), safe_ids, route_w, state.kmax, float(limit), scratch,
-                          intermediate=state.inter, k_table=state.ktab, codebook=state.codebook)
+    _ext.lna2_moe_prefill(x, out, *state.table_list(), ids2, route_w, state.kmax, float(limit), scratch,
+                          intermediate=state.inter, k_table=state.ktab, codebook=state.codebook,
+                          expert_map=expert_map)
     _CALLS["b200"] += 1
     return out
 

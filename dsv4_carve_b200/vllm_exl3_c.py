@@ -20,14 +20,16 @@ Generalisations over the reference, all optional keyword arguments:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
 
 __all__ = [
     "dequant_trellis", "exl3_gemv", "exl3_gemm", "exl3_mgemm", "lna2_moe_decode", "lna2_moe_scratch_bytes",
-    "lna2_moe_max_rows", "lna2_moe_prepare", "lna2_moe_info", "lna2_moe_status",
-    "exl3_linear_scratch_bytes",
+    "lna2_moe_max_rows", "lna2_moe_prepare", "lna2_moe_info", "lna2_moe_status", "lna2_moe_status_word",
+    "lna2_moe_decode_routed", "lna2_moe_prefill", "lna2_moe_prefill_scratch_bytes", "exl3_linear_scratch_bytes",
 ]
 
 _DT = {torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16, torch.float32: _lib.DT_F32}
@@ -246,7 +248,11 @@ def lna2_moe_info(K: int) -> list[int]:
 
 
 def lna2_moe_status(scratch: torch.Tensor, clear: bool = False) -> int:
-    """Device status word of a MoE scratch (0 = healthy).  Synchronizes."""
+    """Device status word of a MoE scratch (0 = healthy).  Synchronizes.
+
+    The word is sticky: kernels only OR bits into it (bit 0 dependency wait
+    timed out, 1 misaligned trellis, 2 bit width out of range, 3 ring wait
+    timed out, 4 plan overflow), until it is cleared here."""
     import ctypes
 
     word = ctypes.c_uint32(0)
@@ -256,6 +262,99 @@ def lna2_moe_status(scratch: torch.Tensor, clear: bool = False) -> int:
     return int(word.value)
 
 
+def lna2_moe_status_word(scratch: torch.Tensor) -> torch.Tensor:
+    """The status word of a MoE (or prefill) scratch as a 1-element int32
+    device tensor, a view that stays valid as long as the scratch: a serving
+    loop can copy it to pinned memory asynchronously (or test it inside a CUDA
+    graph) after a layer, without a synchronization per call."""
+    _check(scratch.is_cuda and scratch.dtype == torch.uint8 and scratch.numel() >= 12,
+           "LNA2 scratch must be a CUDA uint8 buffer")
+    return scratch[8:12].view(torch.int32)
+
+
+def _raise_on_status(scratch: torch.Tensor) -> None:
+    word = lna2_moe_status(scratch, clear=True)
+    if word:
+        raise RuntimeError(f"LNA2 device status word 0x{word:x}: a bounded wait or check failed inside the kernel "
+                           "(bit 0 dependency timeout, 1 misaligned trellis, 2 bad bit width, 3 ring timeout, "
+                           "4 plan overflow); the output of that call is not valid")
+
+
+def check_status_default() -> bool:
+    """EXL3_MOE_CHECK_STATUS=1 makes every MoE call synchronize and raise on a
+    nonzero device status word (a validation mode: one sync per layer)."""
+    return os.environ.get("EXL3_MOE_CHECK_STATUS", "0") not in ("", "0")
+
+
+_IDS_DT = {torch.int32: 0, torch.int64: 1}
+
+
+class _MoeArgs:
+    """Argument checks shared by the MoE entries (lna_moe_ticket.cu:516-553)."""
+
+    def __init__(self, x, out, tables, expert_ids, routing_weights, K, swiglu_limit, scratch, intermediate,
+                 k_table, *, routed: bool, prefill: bool, expert_map=None):
+        _check(x.is_cuda and x.dtype in ((torch.float16, torch.bfloat16, torch.float32) if routed and not prefill
+                                          else (torch.float16, torch.bfloat16)),
+               "LNA2 input must be CUDA fp16 or bf16")
+        _check(x.dim() == 2 and x.size(1) % 128 == 0, "LNA2 input must be [m,hidden] with hidden % 128 == 0")
+        if prefill:
+            _check(x.size(0) >= 1, "LNA2 row count out of range (m >= 1)")
+        else:
+            _check(1 <= x.size(0) <= lna2_moe_max_rows(), "LNA2 row count out of range (1 <= m <= LNA2_MAX_M)")
+        _check(x.is_contiguous(), "LNA2 input must be contiguous")
+        _check(out.is_cuda and out.device == x.device and out.shape == x.shape and out.is_contiguous(),
+               "LNA2 output must match x shape/device and be contiguous")
+        _check(out.dtype in (torch.float16, torch.bfloat16, torch.float32), "LNA2 output must be fp16/bf16/fp32")
+        topk = expert_ids.size(-1) if expert_ids.dim() == 2 else -1
+        id_types = (torch.int32, torch.int64) if routed else (torch.int32,)
+        _check(expert_ids.is_cuda and expert_ids.device == x.device and expert_ids.dtype in id_types
+               and expert_ids.is_contiguous() and expert_ids.dim() == 2 and expert_ids.size(0) == x.size(0)
+               and 1 <= topk <= 16,
+               "LNA2 expert_ids must be contiguous int32 [m,topk]" if not routed
+               else "LNA2 expert_ids must be contiguous int32 or int64 [m,topk]")
+        w_types = (torch.float32, torch.bfloat16, torch.float16) if routed else (torch.float32,)
+        _check(routing_weights.is_cuda and routing_weights.device == x.device and routing_weights.dtype in w_types
+               and routing_weights.is_contiguous() and routing_weights.shape == expert_ids.shape,
+               "LNA2 routing_weights must be contiguous fp32 [m,topk]" if not routed
+               else "LNA2 routing_weights must be contiguous fp32/bf16/fp16 [m,topk]")
+        n_experts = tables[0].numel()
+        _check(1 <= n_experts <= 1024, "LNA2 pointer table has invalid expert count")
+        for t in tables:
+            _check(t.is_cuda and t.device == x.device and t.dtype == torch.int64 and t.is_contiguous()
+                   and t.numel() == n_experts, "LNA2 pointer tables must be contiguous CUDA int64 [experts]")
+        limit = float(swiglu_limit)
+        _check(limit > 0.0 and limit < float("inf"), "LNA2 requires a finite positive SwiGLU limit")
+        inter = int(intermediate)
+        if prefill:
+            need = lna2_moe_prefill_scratch_bytes(x.size(0), topk, x.size(1), inter, n_experts)
+        else:
+            need = int(_lib.load().exl3_moe_scratch_bytes(x.size(0), topk, x.size(1), inter))
+        _check(scratch.is_cuda and scratch.device == x.device and scratch.dtype == torch.uint8
+               and scratch.is_contiguous() and scratch.numel() >= need, "LNA2 scratch too small")
+        if k_table is None:
+            bits = int(K)
+            _check(1 <= bits <= 4, "LNA2 supports K1..K4 in this build")
+            kt_ptr, kmax = None, bits
+        else:
+            _check(k_table.is_cuda and k_table.device == x.device and k_table.dtype == torch.int32
+                   and k_table.is_contiguous() and k_table.numel() == n_experts,
+                   "LNA2 k_table must be contiguous CUDA int32 [experts]")
+            kt_ptr, kmax = k_table.data_ptr(), int(K)
+            bits = kmax
+        map_ptr, n_global = None, 0
+        if expert_map is not None:
+            _check(expert_map.is_cuda and expert_map.device == x.device and expert_map.dtype == torch.int64
+                   and expert_map.dim() == 1 and expert_map.is_contiguous() and expert_map.numel() >= 1,
+                   "EXL3 expert_map must be a contiguous CUDA int64 [n_global] on the hidden-state device")
+            map_ptr, n_global = expert_map.data_ptr(), expert_map.numel()
+        self.topk, self.n_experts, self.limit, self.inter = topk, n_experts, limit, inter
+        self.kt_ptr, self.kmax, self.bits = kt_ptr, kmax, bits
+        self.tables = [t.data_ptr() for t in tables]
+        self.route = _lib.MoeRoute(expert_ids.data_ptr(), _IDS_DT[expert_ids.dtype], routing_weights.data_ptr(),
+                                   _DT[routing_weights.dtype], map_ptr, n_global)
+
+
 def lna2_moe_decode(x: torch.Tensor, out: torch.Tensor,
                     gate_trellis: torch.Tensor, gate_suh: torch.Tensor, gate_svh: torch.Tensor,
                     up_trellis: torch.Tensor, up_suh: torch.Tensor, up_svh: torch.Tensor,
@@ -263,65 +362,71 @@ def lna2_moe_decode(x: torch.Tensor, out: torch.Tensor,
                     expert_ids: torch.Tensor, routing_weights: torch.Tensor, K: int,
                     swiglu_limit: float, scratch: torch.Tensor, *, intermediate: int = 256,
                     k_table: torch.Tensor | None = None, codebook: int = 1,
-                    precise: bool = False, tp_exchange=None) -> torch.Tensor:
+                    precise: bool = False, tp_exchange=None, check_status: bool | None = None) -> torch.Tensor:
     """Routed-expert decode of one layer; writes and returns `out`.
 
     Argument checks follow recipe-lna/lna2/lna_moe_ticket.cu:516-553.  With
     `tp_exchange` (a dsv4_carve_b200.tp.MoeTpExchange), the tensor-parallel
     sum of the layer output over the exchange's ranks is done inside the
-    kernel and every rank's `out` holds the full sum."""
-    _check(x.is_cuda and x.dtype in (torch.float16, torch.bfloat16),
-           "LNA2 input must be CUDA fp16 or bf16")
-    _check(x.dim() == 2 and x.size(1) % 128 == 0, "LNA2 input must be [m,hidden] with hidden % 128 == 0")
-    max_m = lna2_moe_max_rows()
-    _check(1 <= x.size(0) <= max_m, "LNA2 row count out of range (1 <= m <= LNA2_MAX_M)")
-    _check(x.is_contiguous(), "LNA2 input must be contiguous")
-    _check(out.is_cuda and out.device == x.device and out.shape == x.shape and out.is_contiguous(),
-           "LNA2 output must match x shape/device and be contiguous")
-    _check(out.dtype in (torch.float16, torch.bfloat16, torch.float32), "LNA2 output must be fp16/bf16/fp32")
-    topk = expert_ids.size(-1) if expert_ids.dim() == 2 else -1
-    _check(expert_ids.is_cuda and expert_ids.dtype == torch.int32 and expert_ids.is_contiguous()
-           and expert_ids.dim() == 2 and expert_ids.size(0) == x.size(0) and 1 <= topk <= 16,
-           "LNA2 expert_ids must be contiguous int32 [m,topk]")
-    _check(routing_weights.is_cuda and routing_weights.dtype == torch.float32
-           and routing_weights.is_contiguous() and routing_weights.shape == expert_ids.shape,
-           "LNA2 routing_weights must be contiguous fp32 [m,topk]")
+    kernel and every rank's `out` holds the full sum.  `check_status` (default:
+    EXL3_MOE_CHECK_STATUS) synchronizes after the launch and raises
+    RuntimeError if the device status word reports a failed wait or check."""
     tables = (gate_trellis, gate_suh, gate_svh, up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh)
-    n_experts = gate_trellis.numel()
-    _check(1 <= n_experts <= 1024, "LNA2 pointer table has invalid expert count")
-    for t in tables:
-        _check(t.is_cuda and t.device == x.device and t.dtype == torch.int64 and t.is_contiguous()
-               and t.numel() == n_experts, "LNA2 pointer tables must be contiguous CUDA int64 [experts]")
-    limit = float(swiglu_limit)
-    _check(limit > 0.0 and limit < float("inf"), "LNA2 requires a finite positive SwiGLU limit")
-    inter = int(intermediate)
-    need = int(_lib.load().exl3_moe_scratch_bytes(x.size(0), topk, x.size(1), inter))
-    _check(scratch.is_cuda and scratch.device == x.device and scratch.dtype == torch.uint8
-           and scratch.is_contiguous() and scratch.numel() >= need, "LNA2 scratch too small")
-    if k_table is None:
-        bits = int(K)
-        _check(1 <= bits <= 4, "LNA2 supports K1..K4 in this build")
-        kt_ptr, kmax = None, bits
-    else:
-        _check(k_table.is_cuda and k_table.device == x.device and k_table.dtype == torch.int32
-               and k_table.is_contiguous() and k_table.numel() == n_experts,
-               "LNA2 k_table must be contiguous CUDA int32 [experts]")
-        kt_ptr, kmax = k_table.data_ptr(), int(K)
-        bits = kmax
+    a = _MoeArgs(x, out, tables, expert_ids, routing_weights, K, swiglu_limit, scratch, intermediate, k_table,
+                 routed=False, prefill=False)
     with _on_device(x.device):
         if tp_exchange is None:
             _lib.call("exl3_moe_decode", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
-                      x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
-                      kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
+                      x.size(0), x.size(1), a.inter, *a.tables, a.n_experts, a.kt_ptr, a.bits, a.kmax,
+                      int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), a.topk, a.limit,
                       scratch.data_ptr(), scratch.numel(), int(bool(precise)), _stream(x.device))
         else:
             _check(tp_exchange.table.device == x.device and tp_exchange.hidden == x.size(1)
                    and x.size(0) <= tp_exchange.max_rows, "LNA2 TP exchange does not match this call")
             _lib.call("exl3_moe_decode_tp", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
-                      x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
-                      kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
+                      x.size(0), x.size(1), a.inter, *a.tables, a.n_experts, a.kt_ptr, a.bits, a.kmax,
+                      int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), a.topk, a.limit,
                       scratch.data_ptr(), scratch.numel(), int(bool(precise)), tp_exchange.table.data_ptr(),
                       tp_exchange.rank, tp_exchange.world, tp_exchange.max_rows, _stream(x.device))
+        if check_status_default() if check_status is None else check_status:
+            _raise_on_status(scratch)
+    return out
+
+
+def lna2_moe_decode_routed(x: torch.Tensor, out: torch.Tensor,
+                           gate_trellis: torch.Tensor, gate_suh: torch.Tensor, gate_svh: torch.Tensor,
+                           up_trellis: torch.Tensor, up_suh: torch.Tensor, up_svh: torch.Tensor,
+                           down_trellis: torch.Tensor, down_suh: torch.Tensor, down_svh: torch.Tensor,
+                           expert_ids: torch.Tensor, routing_weights: torch.Tensor, K: int,
+                           swiglu_limit: float, scratch: torch.Tensor, *, intermediate: int = 256,
+                           k_table: torch.Tensor | None = None, codebook: int = 1, precise: bool = False,
+                           expert_map: torch.Tensor | None = None, tp_exchange=None,
+                           check_status: bool | None = None) -> torch.Tensor:
+    """lna2_moe_decode on the router's raw outputs, in ONE launch: expert_ids
+    int32 or int64 (global ids when `expert_map` is given), routing_weights
+    fp32 / bf16 / fp16, x fp16 / bf16 / fp32.  The id mapping and casts the
+    reference's plugin runs as torch operations before the kernel
+    (map_topk_to_local and .to(int32) / .to(float32),
+    recipe-lna/vllm_exl3_exl3.py.lna:963-987,1234-1236) happen inside it
+    (exl3_moe_decode_routed)."""
+    tables = (gate_trellis, gate_suh, gate_svh, up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh)
+    a = _MoeArgs(x, out, tables, expert_ids, routing_weights, K, swiglu_limit, scratch, intermediate, k_table,
+                 routed=True, prefill=False, expert_map=expert_map)
+    tp_ptr, tp_rank, tp_world, tp_rows = None, 0, 0, 0
+    if tp_exchange is not None:
+        _check(tp_exchange.table.device == x.device and tp_exchange.hidden == x.size(1)
+               and x.size(0) <= tp_exchange.max_rows, "LNA2 TP exchange does not match this call")
+        tp_ptr, tp_rank = tp_exchange.table.data_ptr(), tp_exchange.rank
+        tp_world, tp_rows = tp_exchange.world, tp_exchange.max_rows
+    import ctypes
+
+    with _on_device(x.device):
+        _lib.call("exl3_moe_decode_routed", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                  x.size(0), x.size(1), a.inter, *a.tables, a.n_experts, a.kt_ptr, a.bits, a.kmax, int(codebook),
+                  ctypes.addressof(a.route), a.topk, a.limit, scratch.data_ptr(), scratch.numel(),
+                  int(bool(precise)), tp_ptr, tp_rank, tp_world, tp_rows, _stream(x.device))
+        if check_status_default() if check_status is None else check_status:
+            _raise_on_status(scratch)
     return out
 
 
@@ -348,53 +453,33 @@ def lna2_moe_prefill(x: torch.Tensor, out: torch.Tensor,
                      down_trellis: torch.Tensor, down_suh: torch.Tensor, down_svh: torch.Tensor,
                      expert_ids: torch.Tensor, routing_weights: torch.Tensor, K: int,
                      swiglu_limit: float, scratch: torch.Tensor, *, intermediate: int = 256,
-                     k_table: torch.Tensor | None = None, codebook: int = 1) -> torch.Tensor:
+                     k_table: torch.Tensor | None = None, codebook: int = 1,
+                     expert_map: torch.Tensor | None = None, check_status: bool | None = None) -> torch.Tensor:
     """Routed-expert layer for prefill chunks on the tensor cores; writes and
     returns `out`.  Same arguments and checks as lna2_moe_decode, any row
     count; the weights enter the MMA rounded to fp16 (the reference's decoded
-    values)."""
-    _check(x.is_cuda and x.dtype in (torch.float16, torch.bfloat16),
-           "LNA2 input must be CUDA fp16 or bf16")
-    _check(x.dim() == 2 and x.size(1) % 128 == 0, "LNA2 input must be [m,hidden] with hidden % 128 == 0")
-    _check(x.size(0) >= 1, "LNA2 row count out of range (m >= 1)")
-    _check(x.is_contiguous(), "LNA2 input must be contiguous")
-    _check(out.is_cuda and out.device == x.device and out.shape == x.shape and out.is_contiguous(),
-           "LNA2 output must match x shape/device and be contiguous")
-    _check(out.dtype in (torch.float16, torch.bfloat16, torch.float32), "LNA2 output must be fp16/bf16/fp32")
-    topk = expert_ids.size(-1) if expert_ids.dim() == 2 else -1
-    _check(expert_ids.is_cuda and expert_ids.dtype == torch.int32 and expert_ids.is_contiguous()
-           and expert_ids.dim() == 2 and expert_ids.size(0) == x.size(0) and 1 <= topk <= 16,
-           "LNA2 expert_ids must be contiguous int32 [m,topk]")
-    _check(routing_weights.is_cuda and routing_weights.dtype == torch.float32
-           and routing_weights.is_contiguous() and routing_weights.shape == expert_ids.shape,
-           "LNA2 routing_weights must be contiguous fp32 [m,topk]")
+    values).  Like lna2_moe_decode_routed it also takes int64 ids, bf16 / fp16
+    routing weights and an `expert_map`, read by the device route plan."""
     tables = (gate_trellis, gate_suh, gate_svh, up_trellis, up_suh, up_svh, down_trellis, down_suh, down_svh)
-    n_experts = gate_trellis.numel()
-    _check(1 <= n_experts <= 1024, "LNA2 pointer table has invalid expert count")
-    for t in tables:
-        _check(t.is_cuda and t.device == x.device and t.dtype == torch.int64 and t.is_contiguous()
-               and t.numel() == n_experts, "LNA2 pointer tables must be contiguous CUDA int64 [experts]")
-    limit = float(swiglu_limit)
-    _check(limit > 0.0 and limit < float("inf"), "LNA2 requires a finite positive SwiGLU limit")
-    inter = int(intermediate)
-    need = lna2_moe_prefill_scratch_bytes(x.size(0), topk, x.size(1), inter, n_experts)
-    _check(scratch.is_cuda and scratch.device == x.device and scratch.dtype == torch.uint8
-           and scratch.is_contiguous() and scratch.numel() >= need, "LNA2 scratch too small")
-    if k_table is None:
-        bits = int(K)
-        _check(1 <= bits <= 4, "LNA2 supports K1..K4 in this build")
-        kt_ptr, kmax = None, bits
-    else:
-        _check(k_table.is_cuda and k_table.device == x.device and k_table.dtype == torch.int32
-               and k_table.is_contiguous() and k_table.numel() == n_experts,
-               "LNA2 k_table must be contiguous CUDA int32 [experts]")
-        kt_ptr, kmax = k_table.data_ptr(), int(K)
-        bits = kmax
+    routed = (expert_map is not None or expert_ids.dtype != torch.int32
+              or routing_weights.dtype != torch.float32)
+    a = _MoeArgs(x, out, tables, expert_ids, routing_weights, K, swiglu_limit, scratch, intermediate, k_table,
+                 routed=routed, prefill=True, expert_map=expert_map)
+    import ctypes
+
     with _on_device(x.device):
-        _lib.call("exl3_moe_prefill", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
-                  x.size(0), x.size(1), inter, *[t.data_ptr() for t in tables], n_experts, kt_ptr, bits,
-                  kmax, int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), topk, limit,
-                  scratch.data_ptr(), scratch.numel(), _stream(x.device))
+        if not routed:
+            _lib.call("exl3_moe_prefill", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                      x.size(0), x.size(1), a.inter, *a.tables, a.n_experts, a.kt_ptr, a.bits, a.kmax,
+                      int(codebook), expert_ids.data_ptr(), routing_weights.data_ptr(), a.topk, a.limit,
+                      scratch.data_ptr(), scratch.numel(), _stream(x.device))
+        else:
+            _lib.call("exl3_moe_prefill_routed", x.data_ptr(), _DT[x.dtype], out.data_ptr(), _DT[out.dtype],
+                      x.size(0), x.size(1), a.inter, *a.tables, a.n_experts, a.kt_ptr, a.bits, a.kmax,
+                      int(codebook), ctypes.addressof(a.route), a.topk, a.limit, scratch.data_ptr(),
+                      scratch.numel(), _stream(x.device))
+        if check_status_default() if check_status is None else check_status:
+            _raise_on_status(scratch)
     return out
 
 

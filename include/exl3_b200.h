@@ -6,9 +6,10 @@
  * device pointers must be on the device that is current on the calling
  * thread.  Every function returns EXL3_OK (0) or an exl3_status code; on
  * failure exl3_last_error() returns a message for the calling thread.  Calls
- * that launch work are asynchronous on `stream` and never allocate, copy or
- * synchronize, so they may be captured in a CUDA graph once the per-device
- * state has been prepared (exl3_*_prepare, or one eager call).
+ * that launch work are asynchronous on `stream`.  The entry points that take
+ * a caller scratch never allocate, copy or synchronize, so they may be
+ * captured in a CUDA graph once the per-device state has been prepared
+ * (exl3_*_prepare, or one eager call).
  *
  * Data formats (the EXL3 on-disk / in-memory layout used by the reference):
  *   trellis  int16 [k/16, n/16, 16*K]   packed trellis words of W' (k = in, n = out)
@@ -148,6 +149,41 @@ int exl3_moe_decode(const void* x, int x_dtype, void* out, int out_dtype,
                     const int32_t* ids, const float* weights, int64_t topk,
                     float swiglu_limit, void* scratch, int64_t scratch_bytes, int precise,
                     void* stream);
+/* Routed-MoE decode taking the router's outputs as the serving layer holds
+ * them.  The reference's plugin turns them into the kernel's int32 local ids
+ * and fp32 weights with torch operations before every layer -- the
+ * global-to-local id mapping map_topk_to_local and the dtype casts
+ * (recipe-lna/vllm_exl3_exl3.py.lna:963-987,1234-1236), three or more small
+ * kernels per layer; here the kernel reads them directly:
+ *   ids          device [m, topk], int32 (ids_dtype 0) or int64 (ids_dtype 1);
+ *   weights      device [m, topk], fp16 / bf16 / fp32 (weights_dtype, EXL3_DTYPE_*);
+ *   expert_map   NULL: ids are local expert ids; else device int64 [n_global]
+ *                mapping a global id to this rank's local id, negative when
+ *                the expert lives on another rank.
+ * A slot is skipped when its id is negative, not below n_global (with a
+ * map), mapped to a negative id, or (after mapping) not below n_experts --
+ * exactly the slots map_topk_to_local sends to its sentinel.  Everything else
+ * is exl3_moe_decode; tp_bufs non-NULL adds the fused tensor-parallel sum of
+ * exl3_moe_decode_tp (tp_rank, tp_world, tp_max_rows as there; ignored when
+ * tp_bufs is NULL). */
+typedef struct exl3_moe_route {
+    const void* ids;
+    int ids_dtype;
+    const void* weights;
+    int weights_dtype;
+    const int64_t* expert_map;
+    int64_t n_global;
+} exl3_moe_route;
+int exl3_moe_decode_routed(const void* x, int x_dtype, void* out, int out_dtype,
+                           int64_t m, int64_t hidden, int64_t inter,
+                           const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
+                           const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
+                           const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh,
+                           int64_t n_experts, const int32_t* k_table, int K, int kmax, int cb,
+                           const exl3_moe_route* route, int64_t topk, float swiglu_limit,
+                           void* scratch, int64_t scratch_bytes, int precise,
+                           const int64_t* tp_bufs, int tp_rank, int tp_world, int64_t tp_max_rows,
+                           void* stream);
 /* Replaces lna2_moe_prepare (recipe-lna/lna2/lna_moe_ticket.cu:494-500):
  * occupancy, grid and kernel attributes for the current device, cached, so
  * that later calls can be captured in a CUDA graph. */
@@ -159,20 +195,27 @@ int exl3_moe_prepare(int kmax);
 int exl3_moe_info(int kmax, int64_t* info);
 
 /* Allocation-free variant of exl3_moe_decode.  No counterpart in the
- * reference.  For callers that may not allocate device memory: code running
- * inside CUDA graph capture, hosts whose device memory belongs to another
- * allocator, callers that cannot take cudaMalloc's synchronization.  Same
- * arguments as exl3_moe_decode minus the scratch: the scratch is an
- * 8 MiB array compiled into the library (EXL3_MOE_STATIC_SCRATCH_BYTES),
- * held on every GPU that loads the library until the process exits.
- * Geometries whose exl3_moe_scratch_bytes() exceeds it are rejected with
- * EXL3_ERR_ARG (8 MiB covers m <= 16 rows at top-8, hidden 4096,
- * intermediate 256, and m <= 4 at intermediate 2048).  Each call clears the
- * array's control region with cudaMemsetAsync on `stream`, then launches.
- * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress) and should come before any stream capture.  All
- * calls on a device share the one array: calls that can overlap on the GPU
- * (different streams without ordering) race and must not be issued. */
+ * reference.  For callers that cannot allocate device memory: a plugin loaded
+ * into a serving process whose device memory belongs to the host's own
+ * caching allocator (it may not cudaMalloc a buffer of its own, and the host
+ * offers it none), and latency-critical callers that cannot take
+ * cudaMalloc's implicit device-wide synchronization.  Same arguments as
+ * exl3_moe_decode minus the scratch: the scratch is an 8 MiB array compiled
+ * into the library (EXL3_MOE_STATIC_SCRATCH_BYTES), held on every GPU that
+ * loads the library until the process exits.  Geometries whose
+ * exl3_moe_scratch_bytes() exceeds it are rejected with EXL3_ERR_ARG (8 MiB
+ * covers m <= 16 rows at top-8, hidden 4096, intermediate 256, and m <= 4 at
+ * intermediate 2048).  Each call clears the array's control region with
+ * cudaMemsetAsync on `stream` (the rest is fully written before it is read),
+ * then launches; the memset sits between consecutive layers, so these calls
+ * do not get the programmatic launch overlap of exl3_moe_decode.  The first
+ * call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current), remembers it for the
+ * process, and should come before any stream capture; after
+ * cudaDeviceReset the remembered address is stale and this entry point must
+ * not be used again in that process.  All calls on a device share the one
+ * array, which keeps the last call's contents: calls that can overlap on the
+ * GPU (different streams without ordering) race and must not be issued. */
 #define EXL3_MOE_STATIC_SCRATCH_BYTES (8 << 20)
 int exl3_moe_decode_noalloc(const void* x, int x_dtype, void* out, int out_dtype,
                             int64_t m, int64_t hidden, int64_t inter,
@@ -246,6 +289,18 @@ int exl3_moe_prefill(const void* x, int x_dtype, void* out, int out_dtype,
                      int64_t n_experts, const int32_t* k_table, int K, int kmax, int cb,
                      const int32_t* ids, const float* weights, int64_t topk,
                      float swiglu_limit, void* scratch, int64_t scratch_bytes, void* stream);
+/* exl3_moe_prefill with the routing inputs of exl3_moe_decode_routed (int32 or
+ * int64 ids, optional expert map, fp16 / bf16 / fp32 weights), read by the
+ * device route plan directly instead of after the plugin's torch mapping and
+ * casts (recipe-lna/vllm_exl3_exl3.py.lna:963-987,1617-1629). */
+int exl3_moe_prefill_routed(const void* x, int x_dtype, void* out, int out_dtype,
+                            int64_t m, int64_t hidden, int64_t inter,
+                            const int64_t* gate_trellis, const int64_t* gate_suh, const int64_t* gate_svh,
+                            const int64_t* up_trellis, const int64_t* up_suh, const int64_t* up_svh,
+                            const int64_t* down_trellis, const int64_t* down_suh, const int64_t* down_svh,
+                            int64_t n_experts, const int32_t* k_table, int K, int kmax, int cb,
+                            const exl3_moe_route* route, int64_t topk, float swiglu_limit,
+                            void* scratch, int64_t scratch_bytes, void* stream);
 
 /* Decode-issue roof: runs the GEMV engine's decode inner loop (window
  * extraction, codebook, split-accumulator MMAs) on 32 weight tiles held in

@@ -47,7 +47,7 @@ def build_oracle(force: bool = False) -> Path:
     srcs = [HERE / "exl3_oracle.c", HERE / "exl3_oracle.h"]
     if force or _stale(ORACLE_SO, srcs):
         _run(["gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", "-std=c11", "-shared",
-              "-fPIC", "-o", str(ORACLE_SO), str(HERE / "exl3_oracle.c"), "-lm"])
+              "-fPIC", "-pthread", "-o", str(ORACLE_SO), str(HERE / "exl3_oracle.c"), "-lm"])
     return ORACLE_SO
 
 

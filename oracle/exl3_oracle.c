@@ -9,8 +9,10 @@
 #include "exl3_oracle.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 /* ---------------------------------------------------------------- halves */
 
@@ -176,21 +178,60 @@ void exo_decode(const int16_t* trellis, int64_t kt, int64_t nt, int K, int cb,
     }
 }
 
-/* W' as doubles: the fp16-rounded weights (exact = 0) or lo + hi (exact = 1). */
-static double* decode_values(const int16_t* trellis, int64_t kt, int64_t nt, int K, int cb, int exact) {
-    const int64_t cols = nt * 16;
-    double* w = (double*) malloc(sizeof(double) * (size_t) (kt * 16 * cols));
-    for (int64_t a = 0; a < kt; ++a)
-        for (int64_t b = 0; b < nt; ++b) {
-            const uint16_t* tile = (const uint16_t*) (trellis + (a * nt + b) * 16 * K);
+/* W' as doubles: the fp16-rounded weights (exact = 0) or lo + hi (exact = 1).
+ * Every weight is computed on its own, so the tile rows are shared out over
+ * host threads (EXO_THREADS, default: the online cores, at most 64); the
+ * result does not depend on the thread count. */
+struct decode_job {
+    const int16_t* trellis;
+    int64_t kt, nt;
+    int K, cb, exact, stride, first;
+    double* w;
+};
+
+static void* decode_rows(void* arg) {
+    const struct decode_job* j = (const struct decode_job*) arg;
+    const int64_t cols = j->nt * 16;
+    for (int64_t a = j->first; a < j->kt; a += j->stride)
+        for (int64_t b = 0; b < j->nt; ++b) {
+            const uint16_t* tile = (const uint16_t*) (j->trellis + (a * j->nt + b) * 16 * j->K);
             for (int t = 0; t < 256; ++t) {
                 int k, n;
                 tile_position(t, &k, &n);
-                const uint32_t win = exo_window(tile, K, t);
-                w[(a * 16 + k) * cols + b * 16 + n] =
-                    exact ? exo_codebook_exact(win, cb) : (double) exo_half_to_float(exo_codebook(win, cb, 0));
+                const uint32_t win = exo_window(tile, j->K, t);
+                j->w[(a * 16 + k) * cols + b * 16 + n] =
+                    j->exact ? exo_codebook_exact(win, j->cb) : (double) exo_half_to_float(exo_codebook(win, j->cb, 0));
             }
         }
+    return NULL;
+}
+
+static int oracle_threads(int64_t rows) {
+    long n = 0;
+    const char* env = getenv("EXO_THREADS");
+    if (env && *env) n = strtol(env, NULL, 10);
+    if (n <= 0) n = sysconf(_SC_NPROCESSORS_ONLN);
+    if (n < 1) n = 1;
+    if (n > 64) n = 64;
+    if (n > rows) n = (long) rows;
+    return (int) n;
+}
+
+static double* decode_values(const int16_t* trellis, int64_t kt, int64_t nt, int K, int cb, int exact) {
+    double* w = (double*) malloc(sizeof(double) * (size_t) (kt * 16 * nt * 16));
+    const int nthr = oracle_threads(kt);
+    struct decode_job jobs[64];
+    pthread_t tids[64];
+    int started[64] = {0};
+    for (int i = 0; i < nthr; ++i) {
+        jobs[i] = (struct decode_job) {trellis, kt, nt, K, cb, exact, nthr, i, w};
+        if (i > 0) started[i] = pthread_create(&tids[i], NULL, decode_rows, &jobs[i]) == 0;
+    }
+    decode_rows(&jobs[0]);
+    for (int i = 1; i < nthr; ++i) {
+        if (started[i]) pthread_join(tids[i], NULL);
+        else decode_rows(&jobs[i]);   /* no thread: do its rows here */
+    }
     return w;
 }
 

@@ -49,3 +49,18 @@ def row_rel(got, want) -> float:
         scale = max(np.abs(want[r]).max(), 1e-30)
         worst = max(worst, float(np.abs(got[r] - want[r]).max() / scale))
     return worst
+
+
+def routed_subset(layer, ids) -> tuple:
+    """(experts as numpy, their bit widths, ids renumbered into that list)
+    for only the experts that `ids` routes to: the oracle then decodes ~30
+    experts of a 256-expert layer instead of all of them.  Ids outside the
+    layer become -1 (skipped, as in the kernel).  The oracle's result does
+    not depend on how experts are numbered: pairs are per (expert, row) and
+    the output sums slots in slot order."""
+    ids = np.asarray(ids.cpu() if hasattr(ids, "cpu") else ids).astype(np.int64)
+    used = sorted({int(e) for e in ids.flatten().tolist() if 0 <= int(e) < layer.E})
+    remap = {e: j for j, e in enumerate(used)}
+    local = np.vectorize(lambda v: remap.get(int(v), -1), otypes=[np.int32])(ids) if ids.size else ids
+    experts = [{p: dense_np(layer.experts[e][p]) for p in ("gate", "up", "down")} for e in used]
+    return experts, [int(layer.kbits[e]) for e in used], np.ascontiguousarray(local, dtype=np.int32)

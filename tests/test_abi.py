@@ -20,7 +20,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert _lib.load().exl3_abi_version() == 1
+    assert _lib.load().exl3_abi_version() == 2
 
 
 def test_scratch_size_queries_are_host_only():

@@ -240,3 +240,162 @@ def test_fused_tp_sum_world_of_one(cuda):
     finally:
         torch.cuda.synchronize(cuda)
         ex.close()
+
+
+# ------------------------------------------------------------------ benchmarked shapes
+@pytest.mark.parametrize("precise", [False, True])
+def test_config2_full_layer(cuda, oracle, precise):
+    """The benchmarked workload itself: config 2 on one GPU (256 experts,
+    hidden 4096, intermediate 2048, T = 4, top-8, K2/K3 MCG).  The layer is
+    generated on the device; the oracle gets only the ~30 routed experts."""
+    from tests.helpers import routed_subset
+
+    E, H, I, T, topk = 256, 4096, 2048, 4, 8
+    L = synth.make_moe_layer(E, H, I, synth.expert_bits(E, 71), 71, device=cuda)
+    ids, w = synth.route_uniform(T, E, topk, seed=72)
+    x = synth.activations(T, H, seed=73)
+    got, scratch = run_kernel(L, x, ids, w, precise=precise)
+    experts, kb, loc = routed_subset(L, ids)
+    want, pairs = oracle.moe(x.numpy(), experts, kb, loc, w.numpy(), 10.0, cb=L.cb, exact=not precise)
+    check(got, want)
+    assert ext.lna2_moe_status(scratch) == 0
+    assert pairs == len({(int(e), r) for r in range(T) for e in ids[r].tolist()})
+
+
+# ------------------------------------------------------------------ the reference's own MoE loop
+def _loop_cases():
+    from tests.golden import make_moe_golden as MGL
+
+    return list(MGL.CASES)
+
+
+@pytest.mark.parametrize("precise", [False, True])
+@pytest.mark.parametrize("name", _loop_cases())
+def test_kernel_matches_reference_loop(cuda, name, precise):
+    """The kernel on the reference loop's fixtures (tests/golden/ref_moe_loop.npz:
+    apply_exl3_python_loop, recipe-lna/vllm_exl3_exl3.py.lna:988-1027, run
+    unchanged over the reference's CPU dequant_trellis + fp32 matmul), fed the
+    loop's own inputs -- global int64 ids and, for the mapped case, the same
+    expert_map -- through lna2_moe_decode_routed.  Weight rounding differs
+    (full fp16 W with truncation there, GEMV form here): max-abs <= 2e-3,
+    per-row relative <= 4e-3."""
+    from pathlib import Path
+
+    from tests.golden import make_moe_golden as MGL
+
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "ref_moe_loop.npz")
+    cpu, _, _, _, _ = MGL.make_case(name)
+    assert MGL.layer_sha(cpu) == str(fx[f"{name}_sha"])
+    L = to_device(cpu, cuda)
+    meta = fx[f"{name}_meta"]
+    bf16 = bool(meta[5])
+    xbits = torch.from_numpy(fx[f"{name}_x"].view(np.int16))
+    x = xbits.view(torch.bfloat16 if bf16 else torch.float16).to(cuda)
+    ids = torch.from_numpy(fx[f"{name}_ids"]).to(cuda)
+    w = torch.from_numpy(fx[f"{name}_w"]).to(cuda)
+    emap = torch.from_numpy(fx[f"{name}_map"]).to(cuda) if f"{name}_map" in fx else None
+    T, topk = ids.shape
+    scratch = torch.zeros(ext.lna2_moe_scratch_bytes(T, topk, L.H, L.I), dtype=torch.uint8, device=cuda)
+    out = torch.empty((T, L.H), dtype=torch.float32, device=cuda)
+    ext.lna2_moe_decode_routed(x, out, *L.table_list(), ids, w, max(L.kbits), float(meta[6]) / 1000.0, scratch,
+                               intermediate=L.I, k_table=L.ktab, codebook=L.cb, precise=precise, expert_map=emap,
+                               check_status=True)
+    want = fx[f"{name}_out"].astype(np.float64)
+    got = out.cpu().numpy()
+    assert max_abs(got, want) <= TOL
+    assert row_rel(got, want) <= 4e-3
+
+
+# ------------------------------------------------------------------ routing inputs on the device
+def test_routed_entry_equals_reference_abi_bitwise(cuda):
+    """lna2_moe_decode_routed with int64 ids and fp32 weights == lna2_moe_decode
+    with int32 ids bit for bit; bf16 / fp16 weights == the reference ABI fed
+    the same values cast to fp32 (the plugin's .to(float32))."""
+    E, H, I, T, topk = 32, 1024, 256, 8, 8
+    L = to_device(layer(E, H, I, synth.expert_bits(E, 13), 13), cuda)
+    ids, w = synth.route_zipf(T, E, topk, seed=14, device=cuda)
+    x = synth.activations(T, H, seed=15, device=cuda)
+    ref, _ = run_kernel(L, x, ids, w)
+    for w_in in (w, w.to(torch.bfloat16), w.to(torch.float16)):
+        base, _ = run_kernel(L, x, ids, w_in.float())
+        out = torch.empty_like(ref)
+        scratch = torch.zeros(ext.lna2_moe_scratch_bytes(T, topk, H, I), dtype=torch.uint8, device=cuda)
+        ext.lna2_moe_decode_routed(x, out, *L.table_list(), ids.long(), w_in, max(L.kbits), 10.0, scratch,
+                                   intermediate=I, k_table=L.ktab, codebook=L.cb)
+        assert torch.equal(out, base)
+        if w_in is w:
+            assert torch.equal(out, ref)
+
+
+def test_expert_map_and_skips_on_device(cuda, oracle):
+    """Global ids through an expert map (half the experts on this rank),
+    plus a negative id, an id past the map and an unmapped expert, against
+    the oracle fed the host-mapped local ids."""
+    E, H, I, T, topk = 16, 1024, 256, 4, 6
+    n_global = 40
+    L0 = layer(E, H, I, synth.expert_bits(E, 17), 17)
+    L = to_device(L0, cuda)
+    g = torch.Generator().manual_seed(18)
+    perm = torch.randperm(n_global, generator=g)
+    emap = torch.full((n_global,), -1, dtype=torch.long)
+    emap[perm[:E]] = torch.arange(E)
+    ids, w = synth.route_uniform(T, n_global, topk, seed=19)
+    ids = ids.long()
+    ids[0, 0] = -3
+    ids[1, 1] = n_global + 5
+    ids[2, 2] = int(perm[E])      # a global expert that lives on another rank
+    x = synth.activations(T, H, seed=20)
+    e = emap.numpy()
+    gid = ids.numpy()
+    loc = np.where((gid >= 0) & (gid < n_global), e[np.clip(gid, 0, n_global - 1)], -1).astype(np.int32)
+    out = torch.empty((T, H), dtype=torch.float32, device=cuda)
+    scratch = torch.zeros(ext.lna2_moe_scratch_bytes(T, topk, H, I), dtype=torch.uint8, device=cuda)
+    ext.lna2_moe_decode_routed(x.to(cuda), out, *L.table_list(), ids.to(cuda), w.to(cuda), max(L.kbits), 10.0,
+                               scratch, intermediate=I, k_table=L.ktab, codebook=L.cb, expert_map=emap.to(cuda))
+    want, _ = run_oracle(oracle, L0, x, torch.from_numpy(loc), w)
+    check(out, want)
+
+
+def test_plugin_dispatch_is_one_launch(cuda, oracle):
+    """apply_moe_decode on the router's raw outputs (int64 global ids, bf16
+    weights, an expert map): exactly one kernel runs for the layer -- no
+    mapping, cast or copy kernels around it -- and the result matches."""
+    from torch.profiler import ProfilerActivity, profile
+
+    E, H, I, T, topk = 16, 1024, 256, 4, 4
+    n_global = 24
+    L0 = layer(E, H, I, synth.expert_bits(E, 22), 22)
+    L = to_device(L0, cuda)
+    state = M.build_moe_state(L.experts, codebook=1)
+    M.prepare(state, cuda, max_rows=8, topk=topk)
+    emap = torch.full((n_global,), -1, dtype=torch.long)
+    emap[torch.arange(E) + 8] = torch.arange(E)       # global ids 8..23 live here
+    ids, w = synth.route_uniform(T, n_global, topk, seed=23)
+    x = synth.activations(T, H, seed=24).to(cuda)
+    ids_d, w_d, emap_d = ids.long().to(cuda), w.to(torch.bfloat16).to(cuda), emap.to(cuda)
+    out = torch.empty((T, H), dtype=torch.float32, device=cuda)
+    M.apply_moe_decode(x, ids_d, w_d, state, expert_map=emap_d, out=out)   # warm
+    torch.cuda.synchronize(cuda)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        M.apply_moe_decode(x, ids_d, w_d, state, expert_map=emap_d, out=out)
+        torch.cuda.synchronize(cuda)
+    kernels = [ev.name for ev in prof.events() if ev.device_type == torch.autograd.DeviceType.CUDA]
+    assert len(kernels) == 1 and "moe_kernel" in kernels[0], kernels
+    gid = ids.numpy()
+    loc = np.where((gid >= 8) & (gid < n_global), gid - 8, -1).astype(np.int32)
+    want, _ = run_oracle(oracle, L0, x.cpu(), torch.from_numpy(loc), w.to(torch.bfloat16).float())
+    check(out, want)
+
+
+def test_status_word_surfaces(cuda):
+    """The status word as a pollable device view (0 after a healthy call) and
+    the synchronizing check, which passes on a healthy call."""
+    E, H, I, T, topk = 8, 512, 128, 2, 2
+    L = to_device(layer(E, H, I, [2] * E, 25), cuda)
+    ids, w = synth.route_uniform(T, E, topk, seed=26)
+    x = synth.activations(T, H, seed=27)
+    out, scratch = run_kernel(L, x, ids, w)
+    word = ext.lna2_moe_status_word(scratch)
+    assert word.dtype == torch.int32 and word.numel() == 1 and int(word.item()) == 0
+    ext.lna2_moe_decode(x.to(cuda), out, *L.table_list(), ids.to(cuda), w.to(cuda), 2, 10.0, scratch,
+                        intermediate=I, k_table=L.ktab, codebook=L.cb, check_status=True)

@@ -174,7 +174,7 @@ def test_exl3_moe_shim(cuda, oracle):
     L0 = layer(E, H, I, [2] * E, 29)
     L = to_device(L0, cuda)
     ids, w = synth.route_uniform(T, E, topk, seed=30)
-    ids[3, 1] = E          # a non-local expert (mapped to n_exp by map_topk_to_local)
+    ids[3, 1] = E          # an id past the local experts: the slot is skipped
     x = synth.activations(T, H, seed=31)
     local = ids.to(cuda).reshape(-1).long()
     flat_token = torch.arange(T, device=cuda).repeat_interleave(topk)
@@ -207,3 +207,53 @@ def test_plugin_dispatch_routes_by_rows(cuda, oracle):
         assert y is not None
         want = run_oracle(oracle, L0, x, ids, w)
         assert row_rel(y.float().cpu().numpy(), want) <= 2e-3
+
+
+@pytest.mark.parametrize("I,rows_checked", [(256, 64), (2048, 8)])
+def test_config4b_shape(cuda, oracle, I, rows_checked):
+    """The config-4b prefill chunk: 512 tokens, bf16 activations N(0,1),
+    top-8 of 256 experts, hidden 4096, K2/K3 MCG, at the TP8 shard's
+    intermediate width (256) and at the full single-GPU width (2048).  The
+    kernel runs all 512 tokens; the oracle checks `rows_checked` of them,
+    spread over the chunk (a token's output depends only on its own routes)."""
+    from tests.helpers import routed_subset
+
+    E, H, T, topk = 256, 4096, 512, 8
+    L = synth.make_moe_layer(E, H, I, synth.expert_bits(E, 81), 81, device=cuda)
+    ids, w = synth.route_uniform(T, E, topk, seed=82)
+    x = synth.activations(T, H, seed=83, dtype=torch.bfloat16)
+    out, scratch = run_prefill(L, x, ids, w)
+    rows = torch.from_numpy(np.linspace(0, T - 1, rows_checked).round().astype(np.int64))
+    experts, kb, loc = routed_subset(L, ids[rows])
+    xa, code = oracle_x(x[rows])
+    want, _ = oracle.moe(xa, experts, kb, loc, w[rows].numpy(), 10.0, cb=L.cb, dtype_code=code, exact=False)
+    check(out[rows.to(cuda)], want)
+    assert ext.lna2_moe_status(scratch) == 0
+
+
+def test_prefill_expert_map_on_device(cuda, oracle):
+    """lna2_moe_prefill with int64 global ids, fp16 routing weights and an
+    expert map, read by the device route plan, against the oracle fed the
+    host-mapped ids."""
+    E, H, I, T, topk = 16, 1024, 256, 80, 4
+    n_global = 32
+    L0 = layer(E, H, I, synth.expert_bits(E, 34), 34)
+    L = to_device(L0, cuda)
+    emap = torch.full((n_global,), -1, dtype=torch.long)
+    emap[1::2] = torch.arange(E)                       # odd global ids live here
+    ids, w = synth.route_uniform(T, n_global, topk, seed=35)
+    ids = ids.long()
+    ids[0, 0] = -1
+    ids[5, 1] = n_global
+    x = synth.activations(T, H, seed=36)
+    w16 = w.to(torch.float16)
+    scratch = torch.empty(ext.lna2_moe_prefill_scratch_bytes(T, topk, H, I, E), dtype=torch.uint8, device=cuda)
+    out = torch.empty((T, H), dtype=torch.float32, device=cuda)
+    ext.lna2_moe_prefill(x.to(cuda), out, *L.table_list(), ids.to(cuda), w16.to(cuda), max(L.kbits), 10.0, scratch,
+                         intermediate=I, k_table=L.ktab, codebook=L.cb, expert_map=emap.to(cuda),
+                         check_status=True)
+    gid = ids.numpy()
+    e = emap.numpy()
+    loc = np.where((gid >= 0) & (gid < n_global), e[np.clip(gid, 0, n_global - 1)], -1).astype(np.int32)
+    want = run_oracle(oracle, L0, x, torch.from_numpy(loc), w16.float())
+    check(out, want)

@@ -190,3 +190,50 @@ def test_moe_oracle_equals_explicit_loop(oracle):
             want[r] += float(w[r, s]) * d
     np.testing.assert_allclose(out, want, rtol=0, atol=1e-9)
     assert pairs == 6   # (0,r0) (3,r0) (5,r1) (2,r1) (0,r2) (1,r2)
+
+
+def reference_loop_cases():
+    from tests.golden import make_moe_golden as MGL
+
+    return list(MGL.CASES)
+
+
+def local_ids(ids: np.ndarray, emap: np.ndarray | None, n_local: int) -> np.ndarray:
+    """Global ids -> local ids, -1 for every slot the plugin's mapping sends
+    to its sentinel (negative, past the map, mapped off this rank, or past the
+    local experts)."""
+    if emap is not None:
+        inside = (ids >= 0) & (ids < emap.size)
+        ids = np.where(inside, emap[np.clip(ids, 0, emap.size - 1)], -1)
+    return np.where((ids >= 0) & (ids < n_local), ids, -1).astype(np.int32)
+
+
+@pytest.mark.parametrize("name", reference_loop_cases())
+def test_moe_oracle_matches_reference_loop(oracle, name):
+    """exo_moe against the reference's own apply_exl3_python_loop
+    (recipe-lna/vllm_exl3_exl3.py.lna:988-1027), run unchanged over the
+    reference's CPU dequant_trellis + fp32 matmul by
+    tests/golden/make_moe_golden.py: duplicates, skipped and unmapped ids, an
+    expert map, the SwiGLU clamp, MUL1, bf16 input, one row.  The loop
+    multiplies x by the fully reconstructed fp16 W (with the reference's
+    truncating fp16 conversion), the oracle runs the GEMV form with
+    nearest-even weights, so the two differ by weight rounding only: max-abs
+    <= 2e-3 (the bound for outputs on unit-scale inputs) and per-row relative
+    <= 4e-3 (measured 2.5e-3 at most, on rows with few valid slots)."""
+    from tests.golden import make_moe_golden as MGL
+    from tests.helpers import moe_np, row_rel
+
+    fx = np.load(GOLD / "ref_moe_loop.npz")
+    layer, x, ids, w, emap = MGL.make_case(name)
+    assert MGL.layer_sha(layer) == str(fx[f"{name}_sha"]), "regenerated layer differs from the fixture's"
+    assert np.array_equal(ids.numpy(), fx[f"{name}_ids"])
+    emap_np = fx[f"{name}_map"] if f"{name}_map" in fx else None
+    loc = local_ids(fx[f"{name}_ids"], emap_np, layer.E)
+    meta = fx[f"{name}_meta"]
+    limit = float(meta[6]) / 1000.0
+    code = 1 if int(meta[5]) else 0
+    want = fx[f"{name}_out"].astype(np.float64)
+    got, _ = oracle.moe(fx[f"{name}_x"], moe_np(layer), layer.kbits, loc, fx[f"{name}_w"], limit, cb=layer.cb,
+                        dtype_code=code)
+    assert np.abs(got - want).max() <= 2e-3
+    assert row_rel(got, want) <= 4e-3

@@ -1,13 +1,19 @@
-"""exl3_moe_decode_noalloc: the routed-MoE layer for callers that may not
-allocate device memory (code inside CUDA graph capture, hosts whose device
-memory belongs to another allocator, callers that cannot take cudaMalloc's
-synchronization).  Its scratch is an 8 MiB array compiled into the library.
+"""exl3_moe_decode_noalloc: the routed-MoE layer for callers that cannot
+allocate device memory -- a plugin loaded into a serving process whose
+device memory belongs to the host's own allocator (it may hand out no buffer
+of its own), and latency-critical callers that cannot take cudaMalloc's
+implicit device-wide synchronization.  Its scratch is an 8 MiB array compiled
+into the library, shared by every call on a device and keeping the previous
+call's contents.
 
-Called through the C ABI twice in a row (the array keeps the first call's
-contents, which the second call must not depend on); each result is compared
-with the existing entry point exl3_moe_decode run with a caller-provided
-scratch, at the MoE tests' tolerance (fp32 output, max-abs 2e-3).  This file
-is collected last on purpose, and passes alone in a fresh process as well.
+Two calls in a row through the C ABI: first a larger geometry (8 rows,
+top-8), then a smaller one with different experts, activations and row
+count (3 rows, top-4), so that anything the second call wrongly took from
+what the first left in the shared array would show.  Each output is compared
+with the existing entry point exl3_moe_decode given a fresh caller scratch:
+both run the same deterministic kernel (fixed-order sums), so they must agree
+bit for bit, which is inside the MoE tests' 2e-3 bound.  This file is
+collected last on purpose, and passes alone in a fresh process as well.
 """
 from __future__ import annotations
 
@@ -19,8 +25,6 @@ import torch
 from dsv4_carve_b200 import _lib, synth
 
 pytestmark = pytest.mark.gpu
-
-TOL = 2e-3
 
 
 def _layer(dev):
@@ -38,24 +42,29 @@ def _args(L, x, out, ids, w):
             ids.data_ptr(), w.data_ptr(), ids.shape[1], ctypes.c_float(10.0))
 
 
+def _with_scratch(lib, L, x, ids, w, stream):
+    T, topk = ids.shape
+    out = torch.empty((T, L.H), dtype=torch.float32, device=x.device)
+    scratch = torch.zeros(lib.exl3_moe_scratch_bytes(T, topk, L.H, L.I), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.exl3_moe_decode(*_args(L, x, out, ids, w), scratch.data_ptr(), scratch.numel(), 0, stream))
+    return out
+
+
 def test_noalloc_matches_scratch_entry_point_twice(cuda):
     lib = _lib.load()
     L = _layer(cuda)
-    T, topk = 4, 4
-    ids, w = synth.route_uniform(T, L.E, topk, seed=32, device=cuda)
-    x = synth.activations(T, L.H, seed=33, device=cuda)
     stream = torch.cuda.current_stream(cuda).cuda_stream
-
-    ref = torch.empty((T, L.H), dtype=torch.float32, device=cuda)
-    scratch = torch.zeros(lib.exl3_moe_scratch_bytes(T, topk, L.H, L.I), dtype=torch.uint8, device=cuda)
-    _lib.check(lib.exl3_moe_decode(*_args(L, x, ref, ids, w), scratch.data_ptr(), scratch.numel(), 0, stream))
-
-    for _ in range(2):
+    calls = [(8, 8, 32), (3, 4, 35)]          # (rows, topk, seed): larger first, then smaller
+    for T, topk, seed in calls:
+        assert lib.exl3_moe_scratch_bytes(T, topk, L.H, L.I) <= _lib.MOE_STATIC_SCRATCH_BYTES
+        ids, w = synth.route_uniform(T, L.E, topk, seed=seed, device=cuda)
+        x = synth.activations(T, L.H, seed=seed + 1, device=cuda)
         got = torch.full((T, L.H), float("nan"), dtype=torch.float32, device=cuda)
         _lib.check(lib.exl3_moe_decode_noalloc(*_args(L, x, got, ids, w), 0, stream))
+        ref = _with_scratch(lib, L, x, ids, w, stream)
         torch.cuda.synchronize(cuda)
         assert torch.isfinite(got).all()
-        assert (got - ref).abs().max().item() <= TOL
+        assert torch.equal(got, ref), (got - ref).abs().max().item()
 
 
 def test_noalloc_rejects_geometry_beyond_its_maximum(cuda):
