@@ -62,4 +62,4 @@ def test_library_is_the_native_path(cuda):
     """The ctypes handle is libexl3b200.so from this tree (no fallback)."""
     lib = _lib.load()
     assert _lib.LIB_PATH.name == "libexl3b200.so"
-    assert lib.exl3_abi_version() == 1
+    assert lib.exl3_abi_version() == 2
