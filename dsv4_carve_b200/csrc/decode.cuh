@@ -156,12 +156,29 @@ __device__ __forceinline__ uint32_t window_f(uint32_t lo32, uint32_t hi32, const
 }
 
 // tile_windows_w with the extraction of window_f (the GEMV engine's decoder).
+// K = 2: the eight windows sit 2 bits apart in one word, so three IMAD-shifted
+// copies (by 2, 4 and 6) put every window at bit 0, 8 or 16 of some copy, where
+// a byte permute takes it: 3 IMAD + 8 ALU instead of 6 + 8 (measured on B200:
+// 5.76 against 5.54 T weights/s for the decode loop).
 template <int K>
 __device__ __forceinline__ void tile_windows_f(const uint32_t (&whi_)[TileFmt<K>::NG],
                                                const uint32_t (&wlo_)[TileFmt<K>::NG], const LaneGeom<K>& g,
                                                const ShiftTable& st, uint32_t (&w)[8]) {
     using F = TileFmt<K>;
     constexpr int G = F::G;
+    if constexpr (K == 2) {
+        const uint32_t lo32 = __funnelshift_r(wlo_[0], whi_[0], g.sh[0]);
+        const uint32_t a2 = lo32 * st.mul[2], a4 = lo32 * st.mul[4], a6 = lo32 * st.mul[6];
+        w[0] = __byte_perm(a2, 0u, 0x4432);     // window 14 bits above the last: bits 16..31 of a2
+        w[1] = __byte_perm(a4, 0u, 0x4432);     // 12
+        w[2] = __byte_perm(a6, 0u, 0x4432);     // 10
+        w[3] = __byte_perm(lo32, 0u, 0x4421);   // 8
+        w[4] = __byte_perm(a2, 0u, 0x4421);     // 6: bits 8..23 of a2
+        w[5] = __byte_perm(a4, 0u, 0x4421);     // 4
+        w[6] = __byte_perm(a6, 0u, 0x4421);     // 2
+        w[7] = lo32 & 0xffffu;                  // 0
+        return;
+    }
 #pragma unroll
     for (int h = 0; h < F::NG; ++h) {
         const uint32_t lo32 = __funnelshift_r(wlo_[h], whi_[h], g.sh[h]);
