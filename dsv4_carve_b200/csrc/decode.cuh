@@ -177,8 +177,7 @@ __device__ __forceinline__ void tile_windows_f(const uint32_t (&whi_)[TileFmt<K>
         w[5] = __byte_perm(a4, 0u, 0x4421);     // 4
         w[6] = __byte_perm(a6, 0u, 0x4421);     // 2
         w[7] = lo32 & 0xffffu;                  // 0
-        return;
-    }
+    } else {
 #pragma unroll
     for (int h = 0; h < F::NG; ++h) {
         const uint32_t lo32 = __funnelshift_r(wlo_[h], whi_[h], g.sh[h]);
@@ -191,6 +190,7 @@ __device__ __forceinline__ void tile_windows_f(const uint32_t (&whi_)[TileFmt<K>
         if constexpr (G > 5) w[h * G + 5] = window_f<(G > 5 ? G - 6 : 0) * K>(lo32, hi32, st);
         if constexpr (G > 6) w[h * G + 6] = window_f<(G > 6 ? G - 7 : 0) * K>(lo32, hi32, st);
         if constexpr (G > 7) w[h * G + 7] = window_f<(G > 7 ? G - 8 : 0) * K>(lo32, hi32, st);
+    }
     }
 }
 

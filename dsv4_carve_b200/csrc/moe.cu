@@ -442,18 +442,20 @@ __device__ void tp_finish_row(const MoeParams& p, uint32_t epoch, int blk, int r
     for (int q = 0; q < 4; ++q) store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
 }
 
-// Phase-B epilogue of (group g, hidden block blk), by one warp: sum the down
-// partials, output transform (lna_moe_ticket.cu:368-378); the last group to
-// finish block blk gathers it for every row in slot order (:409-428).
-// Phase-B block epilogue, part 1: the block's down output of every row of
-// group g -- the k-chunk partials summed in chunk order (or, with a single
-// chunk, the unit's tile straight from shared memory), out-H128 * svh -- into
-// downc.
+// Phase-B block epilogue, part 1 (lna_moe_ticket.cu:368-378): the block's
+// down output of every row of group g -- the k-chunk partials summed in chunk
+// order (or, with a single chunk, the unit's tile straight from shared
+// memory), out-H128 * svh -- into downc.  `sv` holds this lane's four svh
+// values when the caller loaded them ahead (else null).
 __device__ void moe_finish_b_rows(const MoeParams& p, const MoePlan& P, int g, int blk, int lane,
-                                  const float* tile) {
+                                  const float* tile, const uint2* sv) {
     const int e = P.gexp[g];
     const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
-    const __half* dsv = reinterpret_cast<const __half*>(p.tab[8][e]) + blk * kCols;
+    uint2 s4;
+    if (sv != nullptr) s4 = *sv;
+    else s4 = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.tab[8][e]) + blk * kCols + lane * 4));
+    const __half2 s01 = *reinterpret_cast<const __half2*>(&s4.x), s23 = *reinterpret_cast<const __half2*>(&s4.y);
+    const float sc[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
     for (int ri = 0; ri < nrows; ++ri) {
         const int64_t pr = pair0 + ri;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -467,31 +469,20 @@ __device__ void moe_finish_b_rows(const MoeParams& p, const MoePlan& P, int g, i
                 v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
             }
         }
-        out_transform(v, dsv, lane);
+        wht128_warp(v, lane);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = v[q] * kHadNorm * sc[q];
         __stcg(reinterpret_cast<float4*>(p.downc + pr * p.H + blk * kCols + lane * 4),
                make_float4(v[0], v[1], v[2], v[3]));
     }
 }
 
-// Phase-B block epilogue, part 2: count the group's block as done; the last
-// group to finish hidden block blk gathers it for every row, the top-k slots
-// summed in slot order in fp32 (recipe-lna/lna2/lna_moe_ticket.cu:409-428).
-// The slots' rows are loaded eight at a time before any is summed, so their
-// L2 latencies overlap.
-__device__ void moe_finish_b_count(const MoeParams& p, const MoePlan& P, int blk, int lane, uint32_t* cntG,
-                                   uint32_t epoch) {
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-        const uint32_t old = atom_add_release_gpu(&cntG[blk], 1u);
-        last = old == (uint32_t) (P.G - 1);
-        if (last) {
-            atomicExch(&cntG[blk], 0u);
-            fence_acq_rel_gpu();
-        }
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
+// Gather of hidden block blk, once every group has finished it: for every
+// row, the top-k slots summed in slot order in fp32
+// (recipe-lna/lna2/lna_moe_ticket.cu:409-428); with the fused TP sum the
+// rank's partial rows go to the exchange instead.  The slots' rows are
+// loaded eight at a time before any is summed, so their L2 latencies overlap.
+__device__ void moe_gather_block(const MoeParams& p, const MoePlan& P, int blk, int lane, uint32_t epoch) {
     for (int r = 0; r < p.m; ++r) {
         float s[4] = {0.f, 0.f, 0.f, 0.f};
         for (int k0 = 0; k0 < p.topk; k0 += 8) {
@@ -522,6 +513,33 @@ __device__ void moe_finish_b_count(const MoeParams& p, const MoePlan& P, int blk
                 store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
         }
     }
+}
+
+// Gathers hidden block blk if the count whose previous value `old` (lane 0)
+// came back completed it: the last of the G groups resets the counter and
+// gathers.
+__device__ __forceinline__ void moe_gather_if_last(const MoeParams& p, const MoePlan& P, int blk, uint32_t old,
+                                                   int lane, uint32_t* cntG, uint32_t epoch) {
+    int last = 0;
+    if (lane == 0) {
+        last = old == (uint32_t) (P.G - 1);
+        if (last) {
+            atomicExch(&cntG[blk], 0u);
+            fence_acq_rel_gpu();   // acquire every group's down output of the block
+        }
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) moe_gather_block(p, P, blk, lane, epoch);
+}
+
+// Phase-B block epilogue, part 2: count the group's block as done (release:
+// the warp's downc stores first) and gather it when this group was the last.
+__device__ void moe_finish_b_count(const MoeParams& p, const MoePlan& P, int blk, int lane, uint32_t* cntG,
+                                   uint32_t epoch) {
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atom_add_release_gpu(&cntG[blk], 1u);
+    moe_gather_if_last(p, P, blk, old, lane, cntG, epoch);
 }
 
 template <int CB, bool PRECISE>
@@ -714,6 +732,12 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         // the block epilogues, off the consumers' critical path.
         PHASE_DECL
         uint32_t du = 0, uu = 0;
+        // A single-chunk down block's count over the groups is issued after
+        // its epilogue and its result looked at once the next descriptor is
+        // in, so the warp does not wait for the atomic's round trip; nothing
+        // in the layer waits on the gather it may start.
+        int pend_blk = -1;
+        uint32_t pend_old = 0u;     // lane 0
         while (true) {
             const int slot = du % kMoeDQ;
             if (!mbar_wait_lanes(&S.dqf[slot], (du / kMoeDQ) & 1u, status)) break;
@@ -724,23 +748,35 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
             PHASE_MARK(PH_EPI_DESC);
+            if (pend_blk >= 0) {
+                moe_gather_if_last(p, P, pend_blk, pend_old, lane, cntG, S.tp_epoch);
+                pend_blk = -1;
+            }
             if (d[0] < 0) break;
             const int kind = d[0], g = d[1], mat = d[2], blk = d[3], s = d[4], K = d[5];
             if (K == 0) continue;
+            const bool single = kind == 1 && p.nkb == 1;
+            uint2 sv4 = make_uint2(0u, 0u);   // the block's svh, loaded while the tile is computed
+            if (single)
+                sv4 = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.tab[8][P.gexp[g]]) +
+                                                           blk * kCols + lane * 4));
             const int ps = (int) (uu & 1u);
             if (!mbar_wait_lanes(&S.pfull[ps], (uu >> 1) & 1u, status)) break;
             PHASE_MARK(PH_EPI_WAIT);
             const int nrows = __popc(P.gmask[g]), pair0 = P.gpair[g];
             const float* tile = ptile + (size_t) ps * p.m * kCols;
-            if (kind == 1 && p.nkb == 1) {
+            if (single) {
                 // A single k-chunk over I: the tile is the block's whole sum, so it
                 // is finished here without a partial store or a completion count.
                 PHASE_COUNT(PH_FINS_B);
-                moe_finish_b_rows(p, P, g, blk, lane, tile);
+                moe_finish_b_rows(p, P, g, blk, lane, tile, &sv4);
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&S.pempty[ps]);
+                if (lane == 0) {
+                    mbar_arrive(&S.pempty[ps]);
+                    pend_old = atom_add_release_gpu(&cntG[blk], 1u);
+                }
+                pend_blk = blk;
                 ++uu;
-                moe_finish_b_count(p, P, blk, lane, cntG, S.tp_epoch);
                 PHASE_MARK(PH_FIN_B);
                 continue;
             }
@@ -781,11 +817,12 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 PHASE_MARK(PH_FIN_A);
             } else {
                 PHASE_COUNT(PH_FINS_B);
-                moe_finish_b_rows(p, P, g, blk, lane, nullptr);
+                moe_finish_b_rows(p, P, g, blk, lane, nullptr, nullptr);
                 moe_finish_b_count(p, P, blk, lane, cntG, S.tp_epoch);
                 PHASE_MARK(PH_FIN_B);
             }
         }
+        if (pend_blk >= 0) moe_gather_if_last(p, P, pend_blk, pend_old, lane, cntG, S.tp_epoch);
         TL_MARK(5);
         PHASE_FLUSH(lane);
     } else {
