@@ -57,8 +57,9 @@ def parse():
                          "the line adds the whole stack's time per decode step")
     ap.add_argument("--tokens", type=int, default=4)
     ap.add_argument("--route", choices=["uniform", "zipf"], default="uniform")
-    ap.add_argument("--config", choices=["moe", "dense", "prefill"], default="moe",
-                    help="moe: config 2/3 routed-MoE layer (the headline); dense: config 1 K6 linears")
+    ap.add_argument("--config", choices=["moe", "dense", "single", "prefill"], default="moe",
+                    help="moe: config 2/3 routed-MoE layer (the headline); dense: config 1 K6 linears; "
+                         "single: config 0, one 4096 x 4096 K4 3INST linear")
     ap.add_argument("--rows", type=int, default=4, help="dense: activation rows R")
     ap.add_argument("--group", action="store_true",
                     help="dense: the two 4096-input matrices in one grouped launch (exl3_linear_group)")
@@ -540,13 +541,19 @@ class DenseWorkload:
     fp16 N(0,1).  A step applies the three linears to one batch; sets of the
     three matrices are cycled so that steps stream from HBM (8 sets = 176 MB).
     TP: the two 4096-input matrices are column-sharded in whole 128-column
-    blocks, [1536 -> 4096] is row-sharded and its partial output all-reduced."""
+    blocks, [1536 -> 4096] is row-sharded and its partial output all-reduced.
+
+    With --config single (config 0): one [4096 -> 4096] K4 3INST linear per
+    step, R = --rows (1 in the config), 16 matrices cycled (134 MB > L2); with
+    N > 1 it is replicated (every rank runs its own copy, no collective)."""
 
     launches_per_step = 3
     kernel_name = "exl3::linear_kernel"
     metric = "dense EXL3 K6 linear set (config 1: [4096->4096], [4096->1536], [1536->4096]): packed-weight HBM GB/s"
 
     def __init__(self, args, rank, world, dev):
+        if args.config == "single":
+            return self._init_single(args, rank, world, dev)
         import torch
 
         from dsv4_carve_b200 import _lib, synth
@@ -612,6 +619,39 @@ class DenseWorkload:
         self.d2h = self.R * 4096 * 2
         self.uniq = []
 
+    def _init_single(self, args, rank, world, dev):
+        import torch
+
+        from dsv4_carve_b200 import _lib, synth
+        from dsv4_carve_b200 import vllm_exl3_c as ext
+
+        self.torch, self.ext, self.args, self.world, self.dev = torch, ext, args, world, dev
+        self.R = args.rows
+        self.lib = _lib.load()
+        self.single = True
+        self.launches_per_step = 1
+        self.metric = "single EXL3 linear (config 0: [4096->4096], K4, 3INST): packed-weight HBM GB/s"
+        self.sets, self.xs, self.ys, self.argv, self.nbytes = [], [], [], [], []
+        for si in range(16):
+            w = synth.make_dense(4096, 4096, 4, seed=7000 + si, device=dev, cb=synth.CB_3INST)
+            self.sets.append([w])
+        self.scratch = torch.zeros(self.lib.exl3_linear_scratch_bytes(self.R, 4096, 4096, 4), dtype=torch.uint8,
+                                   device=dev)
+        x = synth.activations(self.R, 4096, seed=79, device=dev)
+        for (w,) in self.sets:
+            y = torch.empty((self.R, 4096), dtype=torch.float16, device=dev)
+            self.argv.append([("single", (x.data_ptr(), _lib.DT_F16, self.R, 4096, 4096, w.trellis.data_ptr(), 4,
+                                          synth.CB_3INST, w.suh.data_ptr(), w.svh.data_ptr(), y.data_ptr(),
+                                          _lib.DT_F16, self.scratch.data_ptr(), self.scratch.numel(), 1))])
+            self.xs.append([x, x, x])
+            self.ys.append([y, y, y])
+            self.nbytes.append(w.nbytes() + self.R * 2 * (4096 + 4096))
+        self.h_x = [x.cpu().pin_memory()]
+        self.h_y = torch.empty((self.R, 4096), dtype=torch.float16).pin_memory()
+        self.h2d = self.R * 4096 * 2
+        self.d2h = self.R * 4096 * 2
+        self.uniq = []
+
     def launch(self, i, stream_handle):
         for kind, a in self.argv[i % len(self.argv)]:
             fn = self.lib.exl3_linear_group if kind == "group" else self.lib.exl3_linear
@@ -620,7 +660,7 @@ class DenseWorkload:
                 raise RuntimeError(self.lib.exl3_last_error().decode())
 
     def allreduce(self, out):
-        if self.world > 1:
+        if self.world > 1 and not getattr(self, "single", False):
             self.torch.distributed.all_reduce(out)
 
     @property
@@ -640,10 +680,10 @@ class DenseWorkload:
         timed region's output bit for bit; the fast arithmetic (unrounded
         weights, a second computation) agrees within 2e-3."""
         torch = self.torch
-        a, b, c = self.sets[li]
+        c = self.sets[li][-1]
         xin = self.xs[li][2]
-        again = self.ext.linear_forward(xin, c.trellis, c.suh, c.svh, 6, 0, torch.float16, True)
-        fast = self.ext.linear_forward(xin, c.trellis, c.suh, c.svh, 6, 0, torch.float16, False)
+        again = self.ext.linear_forward(xin, c.trellis, c.suh, c.svh, c.K, 0, torch.float16, True)
+        fast = self.ext.linear_forward(xin, c.trellis, c.suh, c.svh, c.K, 0, torch.float16, False)
         self.allreduce(again)
         self.allreduce(fast)
         torch.cuda.synchronize(self.dev)
@@ -666,6 +706,11 @@ class DenseWorkload:
         si = i % len(self.sets)
         x = self.xs[si][0]
         x.copy_(self.h_x[0], non_blocking=True)
+        if getattr(self, "single", False):
+            (w,) = self.sets[si]
+            y = self.ext.linear_forward(x, w.trellis, w.suh, w.svh, 4, 0, torch.float16, True)
+            self.h_y.copy_(y, non_blocking=True)
+            return (y,)
         a, b, c = self.sets[si]
         ya = self.ext.linear_forward(x, a.trellis, a.suh, a.svh, 6, 0, torch.float16, True)
         yb = self.ext.linear_forward(x, b.trellis, b.suh, b.svh, 6, 0, torch.float16, True)
@@ -678,6 +723,11 @@ class DenseWorkload:
         return self.nbytes[i % len(self.sets)]
 
     def describe(self):
+        if getattr(self, "single", False):
+            return {"workload": "config0_single_linear", "rows": self.R, "K": 4, "codebook": "3INST",
+                    "matrices": ["4096x4096"], "sets_cycled": len(self.sets),
+                    "parallelism": f"{self.world} replicas" if self.world > 1 else "single",
+                    "l2": "16 matrices cycled: 16 x 8.4 MB > 126 MB L2", "precise": True}
         return {"workload": "config1_dense_k6_linear_set", "rows": self.R, "K": 6, "codebook": "3INST",
                 "matrices": ["4096x4096", "4096x1536", "1536x4096"], "sets_cycled": len(self.sets),
                 "parallelism": f"tp{self.world}" if self.world > 1 else "single",
@@ -833,7 +883,8 @@ def main():
         if world > 1:
             torch.distributed.barrier(device_ids=[local])
 
-    wl = {"dense": DenseWorkload, "prefill": PrefillWorkload}.get(args.config, MoeWorkload)(args, rank, world, dev)
+    wl = {"dense": DenseWorkload, "single": DenseWorkload, "prefill": PrefillWorkload}.get(args.config, MoeWorkload)(
+        args, rank, world, dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     for i in range(args.warmup):
@@ -958,7 +1009,7 @@ def main():
             traffic = tr["dram_bytes_per_launch"] / tr["algorithmic_bytes_per_launch"] * (my_bytes / K)
         except Exception:
             traffic = None
-    rows = args.rows if args.config == "dense" else getattr(wl, "rows", args.tokens)
+    rows = args.rows if args.config in ("dense", "single") else getattr(wl, "rows", args.tokens)
     line = {
         "metric": wl.metric or METRIC, "value": all_bytes / (ms_max / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
         "steps": K, "warmup": args.warmup, "ms_per_step": ms_max / K, "us_per_layer": ms_max / K * 1e3,

@@ -101,32 +101,35 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const uint8_t* __restr
 }
 
 // ------------------------------------------------------------------ linear
-// One persistent launch per (<= 32-row) block of rows, the same CTA roles as
-// the routed-MoE kernel: warps 0-7 decode + MMA, warp 8 produces (unit
-// tickets, one 3-D TMA box of weights plus one bulk copy of B fragments per
-// ring stage), warp 9 stores each unit's partial tile, counts completions per
-// 128-column block and finishes the block.  Units are (128-column block, k-chunk)
-// in block-major order.  Before their first unit the consumer warps transform
-// the input once per launch (x -> fp16, * suh in fp16, 128-point Hadamard in
-// fp32 -> fp16) straight into B-fragment order; the producer waits (bounded)
-// for a chunk's fragments before copying them.  The finisher sums a block's
-// chunk partials in fixed order and applies Hadamard * svh and the cast, so
-// results are bitwise reproducible.
+// One persistent launch per (<= 32-row) block of rows.  Warps 0-7 decode +
+// MMA, warp 8 produces (unit tickets, one 3-D TMA box of weights per ring
+// stage), warp 9 stores each unit's partial tile, counts completions per
+// 128-column block and finishes the block.  Units are (128-column block,
+// k-chunk) in block-major order; a CTA's first unit is its block index, the
+// rest come from a ticket counter.
+//
+// Launched with programmatic dependent launch: the producer streams its first
+// unit's weights before griddepcontrol.wait (weights never depend on the
+// preceding kernel), and every access to the input, the scratch and the output
+// comes after it.  The consumers transform the unit's own k-chunk of the input
+// (x -> fp16, * suh in fp16, 128-point Hadamard in fp32 -> fp16) straight into
+// B-fragment order in shared memory, so no unit waits on another CTA's input
+// work.  The finisher sums a block's chunk partials in fixed order and applies
+// Hadamard * svh and the cast, so results are bitwise reproducible.
 constexpr int kLinConsumerWarps = 8;
 constexpr int kLinProducerWarp = 8;
 constexpr int kLinEpilogueWarp = 9;
 constexpr int kLinThreads = 320;
 constexpr int kLinMaxRows = 32;
-constexpr int kLinMaxChunks = 8;             // k-chunks per 128-column block
-constexpr int kLinRingBytes = 98304;         // ring + partial tiles
+constexpr int kLinMaxChunks = 16;            // k-chunks per 128-column block
+constexpr int kLinRingBytes = 98304;         // weight ring + partial tiles + the unit's input fragments
+constexpr int kLinFragBytes = 32768;         // most shared memory the unit's input fragments may take
 constexpr int kLinMaxStages = 12;
 constexpr int kLinDQ = 4;
 constexpr int kLinMaxMats = 8;               // matrices of one grouped launch (shared input)
-// control words: [0] unit ticket [1] retired CTAs [2] status [3] input items,
-// readyP[matrix][chunk] at 16, block counters (over all matrices' 128-column
-// blocks) after them
-constexpr int kLinOffReady = 16;
-constexpr int kLinOffCnt = kLinOffReady + kLinMaxMats * kLinMaxChunks;
+// control words: [0] unit ticket [1] retired CTAs [2] status; block counters
+// (over all matrices' 128-column blocks) from word 16
+constexpr int kLinOffCnt = 16;
 
 // One launch applies nmat matrices (same k, K and codebook) to the same input
 // rows: matrix j has its own trellis map, suh, svh, width n[j] and output
@@ -144,9 +147,8 @@ struct LinearParams {
     void* y[kLinMaxMats];
     int y_dtype;
     int kc, nk;                 // k-chunk per unit, chunk count
-    RingGeom ring;
+    RingGeom ring;              // stages hold weights only (slot_bytes == wpart)
     uint32_t* ctrl;
-    uint32_t* xg;               // B fragments [nmat][k/16][rows][4][FW]
     float* partial;             // [nk][rows][ntot]
 };
 
@@ -157,10 +159,58 @@ struct alignas(128) LinHead {
     uint64_t dqe[kLinDQ];
     uint64_t pfull[2];
     uint64_t pempty[2];
+    uint64_t xfree;             // every consumer warp is done with the previous unit's input fragments
+    uint64_t xready;            // every consumer warp has written its share of this unit's fragments
+    uint64_t fin_bar;           // the epilogue warp has published fin_blk (after its last unit)
     int desc[kLinDQ][4];        // valid, block, chunk
+    int fin_blk;                // block whose rows every warp finishes at the end, or -1
     int last_cta;
 };
 constexpr int kLinHeadBytes = (int) ((sizeof(LinHead) + 127) / 128 * 128);
+
+// Per-CTA timeline of the trace build (-DEXL3_PHASE_CLOCK; %globaltimer ns):
+// entry, past griddepcontrol.wait (consumer warp 0), first unit's input
+// fragments ready, first unit decoded, epilogue's first partial counted,
+// epilogue done, exit.  Read with exl3_linear_timeline_read.
+#ifdef EXL3_PHASE_CLOCK
+static __device__ unsigned long long g_ltl[512][8];
+#define LTL_MARK(i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x < 512) g_ltl[blockIdx.x][i] = globaltimer_ns(); } while (0)
+#else
+#define LTL_MARK(i)
+#endif
+
+// Matrix of launch-wide 128-column block blk.
+__device__ __forceinline__ int lin_matrix(const LinearParams& p, int blk) {
+    int mat = 0;
+    while (mat + 1 < p.nmat && blk >= p.blk0[mat + 1]) ++mat;
+    return mat;
+}
+
+// Row r of block blk's epilogue, by one warp: the k-chunk partials summed in
+// chunk order (all in flight at once), Hadamard * svh, one cast into y.
+__device__ __noinline__ void lin_finish_row(const LinearParams& p, int blk, int r, int lane) {
+    const int mat = lin_matrix(p, blk);
+    const int lb = blk - p.blk0[mat];   // the block within its matrix
+    const float* col0 = p.partial + blk * kCols + lane * 4;
+    float4 a[kLinMaxChunks];
+#pragma unroll
+    for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
+        if (c2 < p.nk) a[c2] = __ldcg(reinterpret_cast<const float4*>(col0 + ((int64_t) c2 * p.rows + r) * p.ntot));
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
+        if (c2 < p.nk) { v[0] += a[c2].x; v[1] += a[c2].y; v[2] += a[c2].z; v[3] += a[c2].w; }
+    out_transform(v, p.svh[mat] + lb * kCols, lane);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) store_out(p.y[mat], p.y_dtype, (int64_t) r * p.n[mat] + lb * kCols + lane * 4 + q, v[q]);
+}
+
+// Bounded rendezvous of the consumer warps on an mbarrier of count 8.
+__device__ __forceinline__ bool lin_rendezvous(uint64_t* bar, uint32_t parity, int lane, uint32_t* status) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+    return mbar_wait_lanes(bar, parity, status);
+}
 
 template <int K, int CB, bool PRECISE>
 __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_constant__ LinearParams p) {
@@ -168,40 +218,40 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
     extern __shared__ __align__(128) uint8_t smem_raw[];
     LinHead& S = *reinterpret_cast<LinHead*>(smem_raw);
     uint8_t* ring = smem_raw + kLinHeadBytes;
+    const int rows = p.rows;
     float* ptile = reinterpret_cast<float*>(ring + (size_t) p.ring.ns * p.ring.slot_bytes);   // [2][rows][128]
+    uint32_t* xfrag = reinterpret_cast<uint32_t*>(ptile + 2 * rows * kCols);                   // [kc/16][rows][4*FW]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t* status = p.ctrl + 2;
-    uint32_t* readyP = p.ctrl + kLinOffReady;
     uint32_t* cnt = p.ctrl + kLinOffCnt;
     const int NB = p.blk0[p.nmat];
     const int total = NB * p.nk;
-    const int64_t xg_mat = (int64_t) (p.k / 16) * p.rows * 4 * FW;   // fragment words per matrix
-    const int rows = p.rows;
 
+    if (tid == 0) LTL_MARK(0);
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < p.ring.ns; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], kLinConsumerWarps); }
         for (int s = 0; s < kLinDQ; ++s) { mbar_init(&S.dqf[s], 1); mbar_init(&S.dqe[s], kLinConsumerWarps + 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&S.pfull[s], kLinConsumerWarps); mbar_init(&S.pempty[s], 1); }
+        mbar_init(&S.xfree, kLinConsumerWarps);
+        mbar_init(&S.xready, kLinConsumerWarps);
+        mbar_init(&S.fin_bar, 1);
+        S.fin_blk = -1;
         fence_barrier_init();
     }
     __syncthreads();
 
     if (warp == kLinProducerWarp) {
         // ------------------------------------------------------------ producer
-        int ticket = claim_ticket(&p.ctrl[0], lane);
+        int ticket = (int) blockIdx.x;   // the grid never exceeds the unit count
         uint32_t it = 0, du = 0;
-        bool ok = true;
-        const int64_t rsb = (int64_t) rows * 16 * FW;          // fragment bytes per k-slice
-        const int bbytes = (int) (kStageSK * rsb);
+        bool ok = true, waited = false;
         const uint32_t wbytes = (uint32_t) (kStageSK * 8 * 32 * K);
         const int nst = p.kc / (16 * kStageSK);
         while (ok) {
             const bool end = ticket >= total;
             const int blk = end ? 0 : ticket / p.nk, s = end ? 0 : ticket % p.nk;   // blk over all matrices
-            int mat = 0;
-            while (mat + 1 < p.nmat && blk >= p.blk0[mat + 1]) ++mat;
-            int next_raw = 0;
-            if (!end && lane == 0) next_raw = (int) atomicAdd(&p.ctrl[0], 1u);
+            const int mat = lin_matrix(p, blk);
             if (lane == 0) {
                 const int slot = du % kLinDQ;
                 ok = mbar_wait(&S.dqe[slot], ((du / kLinDQ) + 1u) & 1u, status);
@@ -215,31 +265,30 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             ++du;
             if (end || !ok) break;
-            if (lane == 0) {
-                wait_counter(&readyP[mat * kLinMaxChunks + s], (uint32_t) (p.kc / kCols * rows), status);
-                fence_proxy_async_global();
-            }
-            __syncwarp();
             const int ks0 = s * (p.kc / 16);
-            const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.xg + mat * xg_mat) + (int64_t) ks0 * rsb;
             for (int st = 0; st < nst && ok; ++st) {
                 const int slot = (int) (it % (uint32_t) p.ring.ns);
                 if (lane == 0) {
                     ok = mbar_wait(&S.empty[slot], ((it / (uint32_t) p.ring.ns) + 1u) & 1u, status);
                     if (ok) {
                         uint8_t* dst = ring + (size_t) slot * p.ring.slot_bytes;
-                        mbar_arrive_expect_tx(&S.full[slot], wbytes + (uint32_t) bbytes);
-                        tma_load_3d(dst, &p.tmap[mat], 0, (blk - p.blk0[mat]) * 8, ks0 + st * kStageSK,
-                                    &S.full[slot]);
-                        bulk_g2s(dst + p.ring.wpart, bsrc + (int64_t) st * bbytes, (uint32_t) bbytes, &S.full[slot]);
+                        mbar_arrive_expect_tx(&S.full[slot], wbytes);
+                        tma_load_3d(dst, &p.tmap[mat], 0, (blk - p.blk0[mat]) * 8, ks0 + st * kStageSK, &S.full[slot]);
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                 if (!ok) break;
                 ++it;
             }
+            if (!waited) {
+                pdl_wait();   // the ticket counter is in the scratch the preceding launch restores
+                waited = true;
+            }
+            int next_raw = 0;
+            if (lane == 0) next_raw = (int) gridDim.x + (int) atomicAdd(&p.ctrl[0], 1u);
             ticket = __shfl_sync(0xffffffffu, next_raw, 0);
         }
+        if (!waited) pdl_wait();
         // no bulk copy may still be writing shared memory when the CTA retires
         if (lane == 0) {
             const uint32_t first = it > (uint32_t) p.ring.ns ? it - (uint32_t) p.ring.ns : 0u;
@@ -248,7 +297,9 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
         }
     } else if (warp == kLinEpilogueWarp) {
         // ------------------------------------------------------------ epilogue
+        pdl_wait();
         uint32_t du = 0, uu = 0;
+        int pend_fin = -1;      // block whose epilogue this CTA owes
         while (true) {
             const int slot = du % kLinDQ;
             if (!mbar_wait_lanes(&S.dqf[slot], (du / kLinDQ) & 1u, status)) break;
@@ -257,6 +308,10 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
             if (!valid) break;
+            if (pend_fin >= 0) {   // more units follow: finish the owed block alone
+                for (int r = 0; r < rows; ++r) lin_finish_row(p, pend_fin, r, lane);
+                pend_fin = -1;
+            }
             const int ps = (int) (uu & 1u);
             if (!mbar_wait_lanes(&S.pfull[ps], (uu >> 1) & 1u, status)) break;
             const float* tile = ptile + (size_t) ps * rows * kCols;
@@ -277,79 +332,87 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
                     fence_acq_rel_gpu();
                 }
             }
+            if (uu == 1) LTL_MARK(4);
             last = __shfl_sync(0xffffffffu, last, 0);
             if (!last) continue;
-            int mat = 0;
-            while (mat + 1 < p.nmat && blk >= p.blk0[mat + 1]) ++mat;
-            const int lb = blk - p.blk0[mat];   // the block within its matrix
-            for (int r = 0; r < rows; ++r) {
-                // all chunk partials of the row in flight at once, summed in chunk order
-                float4 a[kLinMaxChunks];
-#pragma unroll
-                for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
-                    if (c2 < p.nk)
-                        a[c2] = __ldcg(reinterpret_cast<const float4*>(
-                            p.partial + ((int64_t) c2 * rows + r) * p.ntot + blk * kCols + lane * 4));
-                float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int c2 = 0; c2 < kLinMaxChunks; ++c2)
-                    if (c2 < p.nk) { v[0] += a[c2].x; v[1] += a[c2].y; v[2] += a[c2].z; v[3] += a[c2].w; }
-                out_transform(v, p.svh[mat] + lb * kCols, lane);
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    store_out(p.y[mat], p.y_dtype, (int64_t) r * p.n[mat] + lb * kCols + lane * 4 + q, v[q]);
+            if (rows <= 2) {       // nothing worth sharing: finish now
+                for (int r = 0; r < rows; ++r) lin_finish_row(p, blk, r, lane);
+                continue;
             }
+            pend_fin = blk;   // finished when the next descriptor is in (alone) or after the last (shared)
         }
+        // The block this CTA finishes last goes to all its warps: the
+        // consumers have no units left and split its rows with this warp.
+        if (lane == 0) S.fin_blk = pend_fin;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.fin_bar);
+        if (pend_fin >= 0)
+            for (int r = kLinConsumerWarps; r < rows; r += kLinConsumerWarps + 1) lin_finish_row(p, pend_fin, r, lane);
+        LTL_MARK(5);
     } else {
         // ------------------------------------------------------------ consumers
-        // input transform: one (matrix, 128-block of k, row) per item (each
-        // matrix has its own suh); a block's fragments are ready when all its
-        // rows are
-        const int KB = p.k / kCols;
-        while (true) {
-            int item = 0;
-            if (lane == 0) item = (int) atomicAdd(&p.ctrl[3], 1u);
-            item = __shfl_sync(0xffffffffu, item, 0);
-            if (item >= p.nmat * KB * rows) break;
-            const int mat = item / (KB * rows);
-            item -= mat * KB * rows;
-            const int r = item % rows;
-            item /= rows;
-            const int k0 = item * kCols + lane * 4;
-            {
-                float v[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const __half a = load_act_half(p.x, p.x_dtype, (int64_t) r * p.k + k0 + q);
-                    v[q] = __half2float(__hmul(a, p.suh[mat][k0 + q]));
-                }
-                wht128_warp(v, lane);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int kl = lane * 4 + q;
-                    const int ks = item * 8 + (kl >> 4);
-                    store_frag<PRECISE>(p.xg + mat * xg_mat + ((size_t) ks * rows + r) * 4 * FW, kl & 15,
-                                        __float2half_rn(v[q] * kHadNorm));
-                }
-            }
-            __syncwarp();
-            if (lane == 0) {
-                fence_proxy_async_global();
-                atom_add_release_gpu(&readyP[mat * kLinMaxChunks + item / (p.kc / kCols)], 1u);
-            }
-        }
+        pdl_wait();   // the input is the preceding kernel's output
+        if (warp == 0) LTL_MARK(1);
         uint32_t it = 0, du = 0, uu = 0;
         const int t4 = lane & 3, gr = lane >> 2;
         const int RB = row_blocks(rows);
         const int nst = p.kc / (16 * kStageSK);
+        const int cb = p.kc / kCols;                   // 128-blocks of k per unit
         while (true) {
             const int slot = du % kLinDQ;
             if (!mbar_wait_lanes(&S.dqf[slot], (du / kLinDQ) & 1u, status)) break;
-            const int valid = S.desc[slot][0];
+            const int valid = S.desc[slot][0], blk = S.desc[slot][1], s = S.desc[slot][2];
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
             if (!valid) break;
+            // The unit's input chunk into B-fragment order in shared memory, one
+            // (128-block, row) item per warp at a time, once every warp is done
+            // with the previous unit's fragments.
+            if (uu > 0 && !lin_rendezvous(&S.xfree, (uu - 1) & 1u, lane, status)) break;
+            {
+                // items (128-block kb of the chunk, row r), up to four per warp
+                // at a time with all their loads issued before any is used
+                constexpr int kBatch = 4;
+                const int mat = lin_matrix(p, blk);
+                const __half* su = p.suh[mat];
+                const int nitems = cb * rows;
+                for (int i0 = warp; i0 < nitems; i0 += kBatch * kLinConsumerWarps) {
+                    __half xa[kBatch][4], sa[kBatch][4];
+#pragma unroll
+                    for (int b = 0; b < kBatch; ++b) {
+                        const int item = i0 + b * kLinConsumerWarps;
+                        if (item < nitems) {
+                            const int r = item % rows, kb = item / rows;
+                            const int k0 = (s * cb + kb) * kCols + lane * 4;
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                xa[b][q] = load_act_half(p.x, p.x_dtype, (int64_t) r * p.k + k0 + q);
+                                sa[b][q] = su[k0 + q];
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int b = 0; b < kBatch; ++b) {
+                        const int item = i0 + b * kLinConsumerWarps;
+                        if (item >= nitems) break;
+                        const int r = item % rows, kb = item / rows;
+                        float v[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) v[q] = __half2float(__hmul(xa[b][q], sa[b][q]));
+                        wht128_warp(v, lane);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int kl = lane * 4 + q;
+                            const int ks = kb * 8 + (kl >> 4);   // k-slice within the unit
+                            store_frag<PRECISE>(xfrag + ((size_t) ks * rows + r) * 4 * FW, kl & 15,
+                                                __float2half_rn(v[q] * kHadNorm));
+                        }
+                    }
+                }
+            }
+            if (!lin_rendezvous(&S.xready, uu & 1u, lane, status)) break;
+            if (warp == 0 && uu == 0) LTL_MARK(2);
             float acc[4][4];
 #pragma unroll
             for (int a = 0; a < 4; ++a)
@@ -359,7 +422,8 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             unsigned long long ph_wait = 0;   // the dense kernel records no phases
 #endif
             if (!ring_consume_rb<K, CB, PRECISE>(RB, p.ring, ring, S.full, S.empty, it, nst, rows, acc, warp, lane,
-                                                 status PH_FWD)) break;
+                                                 status, xfrag PH_FWD)) break;
+            if (warp == 0 && uu == 0) LTL_MARK(3);
             const int ps = (int) (uu & 1u);
             if (!mbar_wait_lanes(&S.pempty[ps], ((uu >> 1) + 1u) & 1u, status)) break;
             float* tile = ptile + (size_t) ps * rows * kCols;
@@ -378,6 +442,12 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             if (lane == 0) mbar_arrive(&S.pfull[ps]);
             ++uu;
         }
+        // rows of the block the epilogue warp shares out at the end (bounded wait)
+        if (mbar_wait_lanes(&S.fin_bar, 0u, status)) {
+            const int fb = *reinterpret_cast<volatile int*>(&S.fin_blk);
+            if (fb >= 0)
+                for (int r = warp; r < rows; r += kLinConsumerWarps + 1) lin_finish_row(p, fb, r, lane);
+        }
     }
 
     // Retire: the last CTA out restores the control words for the next launch.
@@ -388,15 +458,12 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
         S.last_cta = old == gridDim.x - 1;
     }
     __syncthreads();
-    if (S.last_cta) {
+    if (S.last_cta && tid == 0) {
         __threadfence();
-        for (int i = tid; i < p.nmat * kLinMaxChunks; i += kLinThreads) readyP[i] = 0u;
-        if (tid == 0) {
-            atomicExch(&p.ctrl[0], 0u);
-            atomicExch(&p.ctrl[3], 0u);
-            atomicExch(&p.ctrl[1], 0u);
-        }
+        atomicExch(&p.ctrl[0], 0u);
+        atomicExch(&p.ctrl[1], 0u);
     }
+    if (tid == 0) LTL_MARK(6);
 }
 
 // ------------------------------------------------------------------ host side
@@ -417,6 +484,7 @@ LinPrepared g_lin_prep[64][8][3][2];
 
 template <int K, int CB, bool PRECISE>
 int launch_linear(const LinearParams& p, int units, int smem, cudaStream_t stream) {
+    // programmatic stream serialization: see the kernel's prologue
     auto kern = linear_kernel<K, CB, PRECISE>;
     int dev = 0;
     EXL3_CUDA(cudaGetDevice(&dev));
@@ -439,8 +507,17 @@ int launch_linear(const LinearParams& p, int units, int smem, cudaStream_t strea
         grid_max = pr.grid;
     }
     const int grid = units < grid_max ? units : grid_max;
-    kern<<<grid, kLinThreads, smem, stream>>>(p);
-    EXL3_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned) grid);
+    cfg.blockDim = dim3((unsigned) kLinThreads);
+    cfg.dynamicSmemBytes = (size_t) smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    EXL3_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
     return EXL3_OK;
 }
 
@@ -471,18 +548,22 @@ int launch_linear_any(int K, int cb, bool precise, const LinearParams& p, int un
     return precise ? launch_linear_k<true>(K, cb, p, units, smem, s) : launch_linear_k<false>(K, cb, p, units, smem, s);
 }
 
-// k-chunks per 128-column block: the fewest (dividing k into whole 128-blocks,
-// at most kLinMaxChunks) that give every CTA of a full grid a unit.
-int pick_chunks(int64_t k, int64_t n, int grid) {
+// k-chunks per 128-column block: among the chunk counts that divide k into
+// whole 128-blocks (at most kLinMaxChunks) and keep a unit's input fragments
+// (k/c x rows x fw bytes) within kLinFragBytes, the most that still fit one
+// wave (a CTA per unit: no CTA runs a second unit while its block waits on
+// it), else the fewest allowed.  -1 when none is allowed.
+int pick_chunks(int64_t k, int64_t n, int grid, int64_t rows, int fw) {
     const int kb = (int) (k / 128);
     const int64_t nb = n / 128;
-    int best = 1;
+    int best = -1, fewest = -1;
     for (int c = 1; c <= kb && c <= kLinMaxChunks; ++c) {
         if (kb % c) continue;
-        best = c;
-        if (nb * c >= (int64_t) grid) break;
+        if ((k / c) * rows * fw > kLinFragBytes) continue;
+        if (fewest < 0) fewest = c;
+        if (nb * c <= (int64_t) grid) best = c;
     }
-    return best;
+    return best > 0 ? best : fewest;
 }
 
 int assumed_grid() {
@@ -572,12 +653,14 @@ extern "C" int exl3_dequant(const void* trellis, int64_t kt, int64_t nt, int K, 
     return EXL3_OK;
 }
 
-// Scratch: control words, the input fragments of every matrix (sized for
-// 4-word fragments) and the chunk partials over all matrices' columns.
-static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t ntot, int nmat, int grid) {
-    const int nk = pick_chunks(k, ntot, grid);
-    return EXL3_LINEAR_CTRL_BYTES + align_up((int64_t) nmat * k * rows_blk * 4, 256) +
-           align_up((int64_t) nk * rows_blk * ntot * 4, 256);
+// Scratch: control words and the chunk partials over all matrices' columns
+// (sized for the most chunks either arithmetic can pick).
+static int64_t linear_scratch_for(int64_t rows_blk, int64_t k, int64_t ntot, int grid) {
+    int nk = pick_chunks(k, ntot, grid, rows_blk, 2);
+    const int nk4 = pick_chunks(k, ntot, grid, rows_blk, 4);
+    if (nk4 > nk) nk = nk4;
+    if (nk < 1) nk = kLinMaxChunks;
+    return EXL3_LINEAR_CTRL_BYTES + align_up((int64_t) nk * rows_blk * ntot * 4, 256);
 }
 
 // Scratch for `rows` rows: the tensor-core path's (>= 64 rows, one matrix at a
@@ -596,7 +679,7 @@ static int64_t linear_group_need(int64_t rows, int64_t k, int nmat, const int64_
     }
     if (all_tc) return tc;
     const int64_t rb = rows < kLinMaxRows ? rows : kLinMaxRows;
-    const int64_t g = linear_scratch_for(rb, k, ntot, nmat, grid);
+    const int64_t g = linear_scratch_for(rb, k, ntot, grid);
     return g > tc ? g : tc;
 }
 
@@ -697,23 +780,25 @@ int linear_group_impl(const char* who, const void* x, int x_dtype, int64_t rows,
     p.k = (int) k;
     p.x_dtype = x_dtype;
     p.y_dtype = y_dtype;
-    p.nk = pick_chunks(k, gtot, grid);
+    const int fw = precise ? 2 : 4;
+    p.nk = pick_chunks(k, gtot, grid, rb, fw);
+    EXL3_REQUIRE(p.nk >= 1, EXL3_ERR_UNSUPPORTED, "%s: k = %lld has no k-chunk small enough for %lld rows", who,
+                 (long long) k, (long long) rb);
     p.kc = (int) (k / p.nk);
     uint8_t* sb = static_cast<uint8_t*>(scratch);
     p.ctrl = reinterpret_cast<uint32_t*>(sb);
-    p.xg = reinterpret_cast<uint32_t*>(sb + EXL3_LINEAR_CTRL_BYTES);
-    p.partial = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES + align_up((int64_t) gm * k * rb * 4, 256));
-    const int fw = precise ? 2 : 4;
+    p.partial = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES);
     const int esz_x = x_dtype == 2 ? 4 : 2, esz_y = y_dtype == 2 ? 4 : 2;
     const int64_t units = (gtot / kCols) * p.nk;
     for (int64_t r0 = 0; r0 < rows; r0 += kLinMaxRows) {
         p.rows = (int) ((rows - r0) < kLinMaxRows ? (rows - r0) : kLinMaxRows);
         p.ring.wpart = kStageSK * 8 * 32 * K;
-        p.ring.slot_bytes = p.ring.wpart + kStageSK * p.rows * 16 * fw;
-        const int budget = kLinRingBytes - 2 * p.rows * kCols * 4;
+        p.ring.slot_bytes = p.ring.wpart;
+        const int xbytes = p.kc * p.rows * fw;          // the unit's input fragments
+        const int budget = kLinRingBytes - 2 * p.rows * kCols * 4 - xbytes;
         const int nsl = budget / p.ring.slot_bytes;
         p.ring.ns = nsl < 2 ? 2 : (nsl > kLinMaxStages ? kLinMaxStages : nsl);
-        const int smem = kLinHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * p.rows * kCols * 4;
+        const int smem = kLinHeadBytes + p.ring.ns * p.ring.slot_bytes + 2 * p.rows * kCols * 4 + xbytes;
         EXL3_REQUIRE(smem <= kLinHeadBytes + kLinRingBytes, EXL3_ERR_UNSUPPORTED, "%s: stage too large", who);
         p.x = static_cast<const uint8_t*>(x) + r0 * k * esz_x;
         for (int j = 0; j < gm; ++j) p.y[j] = static_cast<uint8_t*>(gy[j]) + r0 * gn[j] * esz_y;
@@ -724,6 +809,15 @@ int linear_group_impl(const char* who, const void* x, int x_dtype, int64_t rows,
 
 }  // namespace
 }  // namespace exl3
+
+#ifdef EXL3_PHASE_CLOCK
+extern "C" int exl3_linear_timeline_read(unsigned long long* out, int n) {
+    EXL3_REQUIRE(out && n >= 1 && n <= 512 * 8, EXL3_ERR_ARG, "linear timeline: bad output");
+    EXL3_CUDA(cudaDeviceSynchronize());
+    EXL3_CUDA(cudaMemcpyFromSymbol(out, exl3::g_ltl, sizeof(unsigned long long) * n));
+    return EXL3_OK;
+}
+#endif
 
 extern "C" int exl3_linear(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, const void* trellis,
                            int K, int cb, const void* suh, const void* svh, void* y, int y_dtype, void* scratch,

@@ -47,10 +47,13 @@ __device__ __forceinline__ void store_frag(uint32_t* rs, int kk, __half h) {
 
 // Decode + MMA over `nst` ring stages of one unit; bit width K and row-block
 // count RB are compile-time so the inner loop carries no predicated MMAs.
+// The B fragments come from each stage after its weight part, or, when
+// `bext` is given, from that shared-memory array (the unit's fragments,
+// kStageSK k-slices per stage, consecutive).
 template <int K, int RB, int CB, bool PRECISE>
 __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                             uint32_t& it, int nst, int nrows, float (&acc)[4][4], int cwarp,
-                                            int lane, uint32_t* status PH_PARAM) {
+                                            int lane, uint32_t* status, const uint32_t* bext PH_PARAM) {
     using F = TileFmt<K>;
     constexpr int FW = Frag<PRECISE>::FW;
     constexpr int ROWW = 8 * F::WORDS;                 // words per k-slice row (8 tiles)
@@ -84,7 +87,7 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
             phi[h] = base + cwarp * F::WORDS + geom.ihi[h];
             plo[h] = base + cwarp * F::WORDS + geom.ilo[h];
         }
-        const uint32_t* bf = base + p.wpart / 4;
+        const uint32_t* bf = bext != nullptr ? bext + st * kStageSK * bstride : base + p.wpart / 4;
 #pragma unroll
         for (int i = 0; i < kStageSK; ++i) {
             uint32_t whi[F::NG], wlo[F::NG];
@@ -124,12 +127,12 @@ __device__ __forceinline__ bool ring_consume(const RingGeom& p, uint8_t* ring, u
 template <int K, int CB, bool PRECISE>
 __device__ __forceinline__ bool ring_consume_rb(int RB, const RingGeom& p, uint8_t* ring, uint64_t* full,
                                                uint64_t* empty, uint32_t& it, int nst, int nrows, float (&acc)[4][4],
-                                               int cwarp, int lane, uint32_t* status PH_PARAM) {
+                                               int cwarp, int lane, uint32_t* status, const uint32_t* bext PH_PARAM) {
     switch (RB) {
-        case 1: return ring_consume<K, 1, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 2: return ring_consume<K, 2, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 3: return ring_consume<K, 3, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        default: return ring_consume<K, 4, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        case 1: return ring_consume<K, 1, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, bext PH_FWD);
+        case 2: return ring_consume<K, 2, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, bext PH_FWD);
+        case 3: return ring_consume<K, 3, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, bext PH_FWD);
+        default: return ring_consume<K, 4, CB, PRECISE>(p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, bext PH_FWD);
     }
 }
 
@@ -138,10 +141,10 @@ __device__ __forceinline__ bool ring_consume_any(int K, int RB, const RingGeom& 
                                                 uint64_t* empty, uint32_t& it, int nst, int nrows, float (&acc)[4][4],
                                                 int cwarp, int lane, uint32_t* status PH_PARAM) {
     switch (K) {
-        case 1: return ring_consume_rb<1, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 2: return ring_consume_rb<2, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        case 3: return ring_consume_rb<3, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
-        default: return ring_consume_rb<4, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status PH_FWD);
+        case 1: return ring_consume_rb<1, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, nullptr PH_FWD);
+        case 2: return ring_consume_rb<2, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, nullptr PH_FWD);
+        case 3: return ring_consume_rb<3, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, nullptr PH_FWD);
+        default: return ring_consume_rb<4, CB, PRECISE>(RB, p, ring, full, empty, it, nst, nrows, acc, cwarp, lane, status, nullptr PH_FWD);
     }
 }
 

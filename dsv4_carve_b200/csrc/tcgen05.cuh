@@ -1,18 +1,12 @@
 // tcgen05.cuh -- inline-PTX wrappers for the 5th-generation tensor cores
 // (sm_100a) shared by the dense and MoE tensor-core kernels: 2-D TMA loads,
 // tcgen05 MMA / commit / TMEM loads and fences, shared-memory matrix
-// descriptors for the 128-byte swizzle, programmatic dependent launch.
+// descriptors for the 128-byte swizzle.
 #pragma once
 
 #include "engine.cuh"
 
 namespace exl3 {
-
-// Programmatic dependent launch: let the next kernel in the stream start its
-// prologue now / wait until the previous kernel has completed and its writes
-// are visible.
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1, uint64_t* bar) {
     asm volatile(

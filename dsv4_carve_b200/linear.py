@@ -5,9 +5,11 @@ Mirrors the interface the vllm-exl3 plugin uses from exllamav3's LinearEXL3
 recipe-lna/vllm_exl3_exl3.py.lna:1337-1366,1552-1558): constructor
 arguments, ``trellis / suh / svh / K / in_features / out_features /
 mcg_tensor / mul1_tensor`` attributes and ``forward(x, params, out_dtype)``.
-Every row count goes through the GEMV kernel (rows are processed in blocks
-of 32); the reference's reconstruct + hgemm path for > 144 rows is the
-tensor-core prefill path, which this build does not replace yet.
+``forward`` calls the C ABI's exl3_linear, which picks the kernel by row
+count: below 64 rows the GEMV ring kernel (register decode into mma.sync,
+32 rows per pass), from 64 rows the tcgen05 tensor-core path (weights decoded
+once into shared memory, applied to up to 512 rows per pass) -- the B200
+counterpart of the reference's GEMV / reconstruct + hgemm split at 144 rows.
 """
 from __future__ import annotations
 
@@ -33,16 +35,16 @@ class LinearEXL3:
     def __init__(self, config=None, in_features: int | None = None, out_features: int | None = None,
                  scale=None, su=None, sv=None, suh=None, svh=None, trellis=None, mcg=None, mul1=None,
                  bias=None, out_dtype=None, transformers_fix: bool = False, key: str | None = None):
-        assert scale is None, "scale is no longer used"
-        assert su is not None or suh is not None, "either su (packed) or suh (unpacked) is required"
-        assert sv is not None or svh is not None, "either sv (packed) or svh (unpacked) is required"
-        assert trellis is not None, "trellis is required"
-        if su is not None: assert su.dtype == torch.int16, "su is wrong datatype"
-        if sv is not None: assert sv.dtype == torch.int16, "sv is wrong datatype"
-        if suh is not None: assert suh.dtype == torch.half, "suh is wrong datatype"
-        if svh is not None: assert svh.dtype == torch.half, "svh is wrong datatype"
-        assert trellis.dtype == torch.int16, "trellis is wrong datatype"
-        assert len(trellis.shape) == 3, "trellis must have dim = 3"
+        assert scale is None, "EXL3 keeps its scales in svh; a separate scale tensor is not accepted"
+        assert su is not None or suh is not None, "input signs missing: give su (bit-packed) or suh (fp16)"
+        assert sv is not None or svh is not None, "output signs missing: give sv (bit-packed) or svh (fp16)"
+        assert trellis is not None, "the packed trellis tensor is missing"
+        if su is not None: assert su.dtype == torch.int16, "su must be int16 bit words"
+        if sv is not None: assert sv.dtype == torch.int16, "sv must be int16 bit words"
+        if suh is not None: assert suh.dtype == torch.half, "suh must be fp16"
+        if svh is not None: assert svh.dtype == torch.half, "svh must be fp16"
+        assert trellis.dtype == torch.int16, "trellis must be int16"
+        assert len(trellis.shape) == 3, "trellis must be [in/16, out/16, 16*K]"
         if bias is not None and bias.dtype == torch.float:
             bias = bias.to(torch.half)
         self.config = config

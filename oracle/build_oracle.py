@@ -23,7 +23,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
-REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
+# The reference tree, named by the REF_ROOT environment variable; without it
+# the _ref builds are skipped and any already built in oracle/_ref are used.
+REF_ROOT = Path(os.environ["REF_ROOT"]) if os.environ.get("REF_ROOT") else None
 ORACLE_SO = BUILD / "libexl3_oracle.so"
 REF_PIN_SO = REF_OUT / "libexl3_ref_pin.so"
 REF_EXT_NAME = "vllm_exl3_c_ref"
@@ -52,7 +54,7 @@ def build_oracle(force: bool = False) -> Path:
 
 
 def ref_available() -> bool:
-    return (REF_ROOT / "orders/F1-ref/exl3_dequant.cuh").is_file()
+    return REF_ROOT is not None and (REF_ROOT / "orders/F1-ref/exl3_dequant.cuh").is_file()
 
 
 def ref_ext_path() -> Path:
