@@ -69,7 +69,12 @@ int exl3_dequant(const void* trellis, int64_t kt, int64_t nt, int K, int cb,
 
 /* ------------------------------------------------------------------ dense linear
  * y[rows, n] = x[rows, k] . W   (GEMV form: input transform, decode + MMA,
- * output transform).  Replaces vllm_exl3_c.exl3_gemv / exl3_gemm
+ * output transform).  Below 64 rows the kernel is launched with programmatic
+ * stream serialization: its CTAs may start while the previous kernel in the
+ * stream is still running and stream the weights (`trellis`) before they
+ * wait for it; x, the scratch and y are touched only after that kernel has
+ * completed.  A preceding kernel that signals griddepcontrol.launch_dependents
+ * early must therefore not write `trellis` after it signals.  Replaces vllm_exl3_c.exl3_gemv / exl3_gemm
  * (recipe-lna/lna2/bindings.cpp:104-109,135-148), exllamav3_ext.exl3_gemm
  * (recipe-lna/exllamav3/exl3_gemm.cu.lna:336-348) and
  * BC_LinearEXL3.run_alloc as called by LinearEXL3.forward

@@ -1,13 +1,15 @@
-"""Fused tensor-parallel sum of the MoE decode layer on two GPUs.
+"""Fused tensor-parallel sum of the MoE decode layer on 2, 4 and 8 GPUs.
 
-Two ranks (spawned processes, one GPU each, NCCL process group on 127.0.0.1
-for the handle exchange and the comparison) hold the TP=2 shards of one
+N ranks (spawned processes, one GPU each, NCCL process group on 127.0.0.1
+for the handle exchange and the comparison) hold the TP=N shards of one
 layer (recipe-lna/vllm_exl3_exl3.py.lna:855-871 slicing).  Each call of
-exl3_moe_decode_tp must give, on both ranks, the NCCL all-reduce of the two
+exl3_moe_decode_tp must give, on every rank, the NCCL all-reduce of the
 ranks' plain partial outputs (fp32 sums in a different order: max-abs 1e-5),
 and rank 0's result must match the oracle's unsharded layer at the MoE
-tolerance (max-abs 2e-3).  Several calls in a row exercise both epoch
-parities of the exchange buffers.  Skipped with fewer than two GPUs.
+tolerance (max-abs 2e-3); every rank ends with the same bits.  Several calls
+in a row exercise both epoch parities of the exchange buffers; the last one
+goes through the routed entry (int64 global ids and an expert map, the
+plugin's inputs).  Each world size is skipped when fewer GPUs are present.
 """
 from __future__ import annotations
 
@@ -20,7 +22,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-E, H, I_FULL, T, TOPK, CALLS = 16, 1024, 512, 4, 4, 4
+E, H, I_FULL, T, TOPK, CALLS = 16, 1024, 1024, 4, 4, 4
 
 
 def _free_port() -> int:
@@ -50,13 +52,19 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         L.experts = [{k: v.to(dev) for k, v in ex_.items()} for ex_ in cpu.experts]
         L.build_tables()
         ex = MoeTpExchange(None, dev, max_rows=8, hidden=H)
+        emap = torch.arange(E, dtype=torch.long, device=dev)   # every expert on every rank (TP, not EP)
         for it in range(CALLS):
             ids, w = synth.route_uniform(T, E, TOPK, seed=70 + it, device=dev)
             x = synth.activations(T, H, seed=80 + it).to(dev)
             scratch = torch.zeros(ext.lna2_moe_scratch_bytes(T, TOPK, H, L.I), dtype=torch.uint8, device=dev)
             fused = torch.empty((T, H), dtype=torch.float32, device=dev)
-            ext.lna2_moe_decode(x, fused, *L.table_list(), ids, w, 3, 10.0, scratch, intermediate=L.I,
-                                k_table=L.ktab, codebook=L.cb, tp_exchange=ex)
+            if it == CALLS - 1:
+                ext.lna2_moe_decode_routed(x, fused, *L.table_list(), ids.long(), w, 3, 10.0, scratch,
+                                           intermediate=L.I, k_table=L.ktab, codebook=L.cb, expert_map=emap,
+                                           tp_exchange=ex)
+            else:
+                ext.lna2_moe_decode(x, fused, *L.table_list(), ids, w, 3, 10.0, scratch, intermediate=L.I,
+                                    k_table=L.ktab, codebook=L.cb, tp_exchange=ex)
             plain = torch.empty_like(fused)
             ext.lna2_moe_decode(x, plain, *L.table_list(), ids, w, 3, 10.0, scratch, intermediate=L.I,
                                 k_table=L.ktab, codebook=L.cb)
@@ -75,22 +83,28 @@ def _worker(rank: int, world: int, port: int, q) -> None:
     q.put(out)
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_tp_sum_two_ranks(oracle):
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_tp_sum(oracle, world):
     import torch.multiprocessing as mp
 
     from dsv4_carve_b200 import synth
     from tests.helpers import max_abs, moe_np, oracle_x
 
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
     try:
-        for _ in range(2):
+        for _ in range(world):
             r = q.get(timeout=240)
             results[r["rank"]] = r
     finally:
@@ -98,7 +112,7 @@ def test_fused_tp_sum_two_ranks(oracle):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    assert set(results) == {0, 1}
+    assert set(results) == set(range(world))
     for r in results.values():
         assert r["error"] is None, r["error"]
         assert all(s == 0 for s in r["status"]), r["status"]
@@ -112,4 +126,5 @@ def test_fused_tp_sum_two_ranks(oracle):
                              exact=True)
         got0 = results[0]["fused"][it]
         assert max_abs(got0, want) <= 2e-3
-        assert (got0 == results[1]["fused"][it]).all()
+        for r in range(1, world):
+            assert (got0 == results[r]["fused"][it]).all()
