@@ -324,13 +324,24 @@ __device__ void moe_finish_a(const MoeParams& p, const MoePlan& P, int g, int bl
     for (int ri = 0; ri < nrows; ++ri) {
         const int64_t pr = pair0 + ri;
         float gv[4] = {0.f, 0.f, 0.f, 0.f}, uv[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c2 = 0; c2 < p.nka; ++c2) {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(
-                p.partA + ((pr * 2 + 0) * p.nka + c2) * p.I + blk * kCols + lane * 4));
-            const float4 b = __ldcg(reinterpret_cast<const float4*>(
-                p.partA + ((pr * 2 + 1) * p.nka + c2) * p.I + blk * kCols + lane * 4));
-            gv[0] += a.x; gv[1] += a.y; gv[2] += a.z; gv[3] += a.w;
-            uv[0] += b.x; uv[1] += b.y; uv[2] += b.z; uv[3] += b.w;
+        // two chunks of gate and of up at a time (four loads in flight), summed
+        // in chunk order
+        for (int c0 = 0; c0 < p.nka; c0 += 2) {
+            float4 a[2], b[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (c0 + j < p.nka) {
+                    a[j] = __ldcg(reinterpret_cast<const float4*>(
+                        p.partA + ((pr * 2 + 0) * p.nka + c0 + j) * p.I + blk * kCols + lane * 4));
+                    b[j] = __ldcg(reinterpret_cast<const float4*>(
+                        p.partA + ((pr * 2 + 1) * p.nka + c0 + j) * p.I + blk * kCols + lane * 4));
+                }
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (c0 + j < p.nka) {
+                    gv[0] += a[j].x; gv[1] += a[j].y; gv[2] += a[j].z; gv[3] += a[j].w;
+                    uv[0] += b[j].x; uv[1] += b[j].y; uv[2] += b[j].z; uv[3] += b[j].w;
+                }
         }
         out_transform(gv, gsv, lane);
         out_transform(uv, usv, lane);
