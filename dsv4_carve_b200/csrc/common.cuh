@@ -179,6 +179,12 @@ __device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t* p, uint32_t v
     return old;
 }
 
+// Add without a return value, ordered after this thread's earlier writes
+// (and those a preceding warp or CTA barrier made it observe).
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 // Spin (bounded) until *ctr >= target.  Returns false on timeout.

@@ -69,7 +69,7 @@ constexpr int kMoeProducerWarp = 8;
 constexpr int kMoeEpilogueWarp = 9;
 constexpr int kMoeThreads = 320;
 // Control region (uint32 words).  ctrl[0] unit ticket, [1] retired CTAs,
-// [2] status word, [3] P-item counter.  Then the per-group counters.
+// [2] status word, [3] unused.  Then the per-group counters.
 constexpr int kCtrlWords = 16;
 constexpr int kOffCntA = kCtrlWords;                                  // [group][I block]
 constexpr int kOffReadyP = kOffCntA + kMoeMaxSlots * kNBImax;          // [group][2][hidden chunk]
@@ -488,69 +488,48 @@ __device__ void moe_finish_b_rows(const MoeParams& p, const MoePlan& P, int g, i
     }
 }
 
-// Gather of hidden block blk, once every group has finished it: for every
-// row, the top-k slots summed in slot order in fp32
-// (recipe-lna/lna2/lna_moe_ticket.cu:409-428); with the fused TP sum the
-// rank's partial rows go to the exchange instead.  The slots' rows are
-// loaded eight at a time before any is summed, so their L2 latencies overlap.
-__device__ void moe_gather_block(const MoeParams& p, const MoePlan& P, int blk, int lane, uint32_t epoch) {
-    for (int r = 0; r < p.m; ++r) {
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k0 = 0; k0 < p.topk; k0 += 8) {
-            float4 d[8];
-            float wv[8];
-            bool ok[8];
+// Row r of hidden block blk of the layer output, by one warp (4 values per
+// lane), once every group has finished the block: the top-k slots summed in
+// slot order in fp32 (recipe-lna/lna2/lna_moe_ticket.cu:409-428); with the
+// fused TP sum the rank's partial row goes to the exchange instead.  The
+// slots' rows are loaded eight at a time before any is summed, so their L2
+// latencies overlap.
+__device__ void moe_gather_row(const MoeParams& p, const MoePlan& P, int blk, int r, int lane, uint32_t epoch) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < p.topk; k0 += 8) {
+        float4 d[8];
+        float wv[8];
+        bool ok[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int k = k0 + j;
-                const int pr = k < p.topk ? (int) P.slotpair[r * p.topk + k] : -1;
-                ok[j] = pr >= 0;
-                wv[j] = ok[j] ? route_weight(p.route, r * p.topk + k) : 0.f;
-                d[j] = __ldcg(reinterpret_cast<const float4*>(p.downc + (int64_t) (ok[j] ? pr : 0) * p.H +
-                                                               blk * kCols + lane * 4));
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (ok[j]) {
-                    s[0] += wv[j] * d[j].x; s[1] += wv[j] * d[j].y; s[2] += wv[j] * d[j].z; s[3] += wv[j] * d[j].w;
-                }
-            }
+        for (int j = 0; j < 8; ++j) {
+            const int k = k0 + j;
+            const int pr = k < p.topk ? (int) P.slotpair[r * p.topk + k] : -1;
+            ok[j] = pr >= 0;
+            wv[j] = ok[j] ? route_weight(p.route, r * p.topk + k) : 0.f;
+            d[j] = __ldcg(reinterpret_cast<const float4*>(p.downc + (int64_t) (ok[j] ? pr : 0) * p.H +
+                                                           blk * kCols + lane * 4));
         }
-        if (p.tp_world > 0) {
-            tp_push_row(p, epoch, blk, lane, r, s);
-        } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
+        for (int j = 0; j < 8; ++j) {
+            if (ok[j]) {
+                s[0] += wv[j] * d[j].x; s[1] += wv[j] * d[j].y; s[2] += wv[j] * d[j].z; s[3] += wv[j] * d[j].w;
+            }
         }
     }
-}
-
-// Gathers hidden block blk if the count whose previous value `old` (lane 0)
-// came back completed it: the last of the G groups resets the counter and
-// gathers.
-__device__ __forceinline__ void moe_gather_if_last(const MoeParams& p, const MoePlan& P, int blk, uint32_t old,
-                                                   int lane, uint32_t* cntG, uint32_t epoch) {
-    int last = 0;
-    if (lane == 0) {
-        last = old == (uint32_t) (P.G - 1);
-        if (last) {
-            atomicExch(&cntG[blk], 0u);
-            fence_acq_rel_gpu();   // acquire every group's down output of the block
-        }
+    if (p.tp_world > 0) {
+        tp_push_row(p, epoch, blk, lane, r, s);
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            store_out(p.out, p.out_dtype, (int64_t) r * p.H + blk * kCols + lane * 4 + q, s[q]);
     }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) moe_gather_block(p, P, blk, lane, epoch);
 }
 
 // Phase-B block epilogue, part 2: count the group's block as done (release:
-// the warp's downc stores first) and gather it when this group was the last.
-__device__ void moe_finish_b_count(const MoeParams& p, const MoePlan& P, int blk, int lane, uint32_t* cntG,
-                                   uint32_t epoch) {
+// the warp's downc stores first).  The gather waits for the count at retire.
+__device__ __forceinline__ void moe_finish_b_count(int blk, int lane, uint32_t* cntG) {
     __syncwarp();
-    uint32_t old = 0;
-    if (lane == 0) old = atom_add_release_gpu(&cntG[blk], 1u);
-    moe_gather_if_last(p, P, blk, old, lane, cntG, epoch);
+    if (lane == 0) red_add_release_gpu(&cntG[blk], 1u);
 }
 
 template <int CB, bool PRECISE>
@@ -743,12 +722,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         // the block epilogues, off the consumers' critical path.
         PHASE_DECL
         uint32_t du = 0, uu = 0;
-        // A single-chunk down block's count over the groups is issued after
-        // its epilogue and its result looked at once the next descriptor is
-        // in, so the warp does not wait for the atomic's round trip; nothing
-        // in the layer waits on the gather it may start.
-        int pend_blk = -1;
-        uint32_t pend_old = 0u;     // lane 0
         while (true) {
             const int slot = du % kMoeDQ;
             if (!mbar_wait_lanes(&S.dqf[slot], (du / kMoeDQ) & 1u, status)) break;
@@ -759,10 +732,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
             PHASE_MARK(PH_EPI_DESC);
-            if (pend_blk >= 0) {
-                moe_gather_if_last(p, P, pend_blk, pend_old, lane, cntG, S.tp_epoch);
-                pend_blk = -1;
-            }
             if (d[0] < 0) break;
             const int kind = d[0], g = d[1], mat = d[2], blk = d[3], s = d[4], K = d[5];
             if (K == 0) continue;
@@ -784,9 +753,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&S.pempty[ps]);
-                    pend_old = atom_add_release_gpu(&cntG[blk], 1u);
+                    red_add_release_gpu(&cntG[blk], 1u);
                 }
-                pend_blk = blk;
                 ++uu;
                 PHASE_MARK(PH_FIN_B);
                 continue;
@@ -829,24 +797,23 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             } else {
                 PHASE_COUNT(PH_FINS_B);
                 moe_finish_b_rows(p, P, g, blk, lane, nullptr, nullptr);
-                moe_finish_b_count(p, P, blk, lane, cntG, S.tp_epoch);
+                moe_finish_b_count(blk, lane, cntG);
                 PHASE_MARK(PH_FIN_B);
             }
         }
-        if (pend_blk >= 0) moe_gather_if_last(p, P, pend_blk, pend_old, lane, cntG, S.tp_epoch);
         TL_MARK(5);
         PHASE_FLUSH(lane);
     } else {
         // ------------------------------------------------------------ consumers
-        // Phase P: input transforms, claimed one warp at a time.
+        // Phase P: input transforms, item i to consumer warp i of the grid
+        // (strided).  Every CTA reaches this point right after its dependency
+        // wait, so a fixed share needs no claim: a shared claim counter cost
+        // thousands of same-address atomics at the start of every layer.
         PHASE_DECL
         const int NKB = p.H / kCols;
         const int PI = G * 2 * NKB;
-        while (true) {
-            int item = 0;
-            if (lane == 0) item = (int) atomicAdd(&p.ctrl[3], 1u);
-            item = __shfl_sync(0xffffffffu, item, 0);
-            if (item >= PI) break;
+        const int nw = (int) gridDim.x * kMoeConsumerWarps;
+        for (int item = (int) blockIdx.x * kMoeConsumerWarps + warp; item < PI; item += nw) {
             const int g = item / (2 * NKB);
             const int r = item % (2 * NKB);
             const int mat = r / NKB, kb = r % NKB;
@@ -923,13 +890,25 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         S.retire_rank = (int) old;
     }
     __syncthreads();
-    if (p.tp_world > 0 && G > 0) {
-        // TP sum: the k-th CTA to retire (its units are done and no ticket is
-        // left, so its waits hold up nothing) finishes output blocks k,
-        // k + grid, ..., one row per warp at a time.
+    if (G > 0) {
+        // Gather (and with TP the sum over ranks): the k-th CTA to retire --
+        // its units are done and no ticket is left, so its waits hold up
+        // nothing -- takes output blocks k, k + grid, ...: once every group
+        // has counted the block, all ten warps gather one row each, so the
+        // rows' L2 round trips overlap instead of running one after another.
         bool ok = true;
-        for (int blk = S.retire_rank; blk < NBH; blk += (int) gridDim.x)
-            for (int r = warp; r < p.m; r += kMoeThreads / 32) tp_finish_row(p, S.tp_epoch, blk, r, lane, ok);
+        for (int blk = S.retire_rank; blk < NBH; blk += (int) gridDim.x) {
+            int done = 1;
+            if (tid == 0) {
+                done = wait_counter(&cntG[blk], (uint32_t) G, status) ? 1 : 0;
+                atomicExch(&cntG[blk], 0u);   // every group has counted: restore for the next launch
+                fence_acq_rel_gpu();          // acquire every group's down output of the block
+            }
+            if (!__syncthreads_and(done)) break;
+            for (int r = warp; r < p.m; r += kMoeThreads / 32) moe_gather_row(p, P, blk, r, lane, S.tp_epoch);
+            if (p.tp_world > 0)
+                for (int r = warp; r < p.m; r += kMoeThreads / 32) tp_finish_row(p, S.tp_epoch, blk, r, lane, ok);
+        }
         ok = __all_sync(0xffffffffu, ok);
         if (!ok && lane == 0) set_error(status, ERR_DEP_TIMEOUT);
     }
@@ -940,7 +919,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
         for (int i = tid; i < G * kMoeMaxNkb; i += kMoeThreads) readyB[i] = 0u;
         if (tid == 0) {
             atomicExch(&p.ctrl[0], 0u);
-            atomicExch(&p.ctrl[3], 0u);
             atomicExch(&p.ctrl[1], 0u);
             // the next launch exchanges under the next epoch
             if (p.tp_world > 0) atomicExch(reinterpret_cast<uint32_t*>(p.tp_bufs[p.tp_rank]), S.tp_epoch);
