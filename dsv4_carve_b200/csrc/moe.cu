@@ -95,7 +95,7 @@ enum {
     PH_FIN_A,          // epilogue: phase-A block epilogue
     PH_FIN_B,          // epilogue: phase-B block epilogue + gather
     PH_PROD_DESC,      // producer: ticket + descriptor publish
-    PH_PROD_DEP,       // producer: tensor map + waiting for input fragments
+    PH_PROD_DEP,       // producer: waiting for input fragments
     PH_PROD_SLOT,      // producer: waiting for ring slots
     PH_PROD_ISSUE,     // producer: issuing copies
     PH_EPI_DESC,       // epilogue: waiting for a descriptor
@@ -105,6 +105,7 @@ enum {
     PH_FINS_A,         // count of phase-A epilogues
     PH_FINS_B,         // count of phase-B epilogues
     PH_TOTAL,          // cycles from kernel start to warp exit
+    PH_PROD_TMAP,      // producer: pointing the unit's tensor map at its matrix
     PH_N
 };
 static __device__ unsigned long long g_phase[PH_N];
@@ -658,6 +659,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 tmap_publish(gtm, &S.tmap);
                 if (lane == 0) tmap_acquire(gtm);
             }
+            PHASE_MARK(PH_PROD_TMAP);
             // The unit's input fragments must be complete before they are copied.
             if (lane == 0) {
                 if (kind == 0) wait_counter(&readyP[(g * 2 + mat) * kMoeMaxNka + s], (uint32_t) (p.kca / kCols), status);
