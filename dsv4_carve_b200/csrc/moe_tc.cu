@@ -138,6 +138,7 @@ struct PfParams {
     int E, H, I;
     float limit;
     uint32_t* ctrl;
+    ShiftTable st;                        // IMAD shift multipliers of the window extraction
     PfPlan plan;
     __half* xd;
     float* dn;
@@ -396,8 +397,8 @@ __global__ void __launch_bounds__(256) pf_input_kernel(const void* x, int x_dtyp
 // stmatrix.x4 into the K-major 128-byte-swizzled A tile (lane l gives the
 // address of row (l % 8) + 8 (l / 16), 8-element chunk (l / 8) % 2).
 template <int K, int CB, int MODE>
-__device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, int ksteps, uint32_t& gs, int warp,
-                               int lane, uint32_t* status PFC_PARAM) {
+__device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, int ksteps, uint32_t& gs,
+                               const ShiftTable& st, int warp, int lane, uint32_t* status PFC_PARAM) {
     using F = TileFmt<K>;
     constexpr int NI = MODE == 0 ? 4 : 2;
     const LaneGeom<K> geom = lane_geom<K>(lane);
@@ -412,20 +413,27 @@ __device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, i
         off[ii] = (uint32_t) (m * (128 * 128) + row * 128 + ((chunk ^ (row & 7)) << 4));
     }
     const uint32_t abase = smem_u32(Abuf);
+    // ring positions as running counters (one division per unit, not per step)
+    int ws = (int) (gs % kPfWStages), as = (int) (gs % kPfAStages);
+    uint32_t wph = (gs / kPfWStages) & 1u, aph = (gs / kPfAStages) & 1u;
     for (int s = 0; s < ksteps; ++s, ++gs) {
-        const int ws = gs % kPfWStages, as = gs % kPfAStages;
         PFC_RESET();
-        if (!mbar_wait_lanes(&H.wfull[ws], (gs / kPfWStages) & 1u, status)) return false;
+        if (!mbar_wait_lanes(&H.wfull[ws], wph, status)) return false;
         PFC_MARK(PF_DEC_W);
-        if (!mbar_wait_lanes(&H.sfree[as], ((gs / kPfAStages) + 1u) & 1u, status)) return false;
+        if (!mbar_wait_lanes(&H.sfree[as], aph ^ 1u, status)) return false;
         PFC_MARK(PF_DEC_AFREE);
         const uint32_t* wst = reinterpret_cast<const uint32_t*>(Wring + ws * kPfWStage);
         const uint32_t a = abase + (uint32_t) (as * kPfAStage);
 #pragma unroll
         for (int ii = 0; ii < NI; ++ii) {
             const uint32_t* t = wst + ((m * 4 + i0 + ii) * 8 + ntile) * F::WORDS;
-            uint32_t w[8], xv[8];
-            tile_windows<K>(t, geom, w);
+            uint32_t whi[F::NG], wlo[F::NG], w[8], xv[8];
+#pragma unroll
+            for (int h = 0; h < F::NG; ++h) {
+                whi[h] = t[geom.ihi[h]];
+                wlo[h] = t[geom.ilo[h]];
+            }
+            tile_windows_f<K>(whi, wlo, geom, st, w);
 #pragma unroll
             for (int j = 0; j < 8; ++j) xv[j] = codebook_pair<CB>(w[j]);
             stmatrix_x4(a + off[ii], round_pair(xv[0], xv[1]), round_pair(xv[2], xv[3]), round_pair(xv[4], xv[5]),
@@ -437,26 +445,28 @@ __device__ bool pf_decode_unit(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, i
             mbar_arrive(&H.aready[as]);
             mbar_arrive(&H.wempty[ws]);
         }
+        if (++ws == kPfWStages) { ws = 0; wph ^= 1u; }
+        if (++as == kPfAStages) { as = 0; aph ^= 1u; }
     }
     return true;
 }
 
 template <int CB, int MODE>
-__device__ bool pf_decode_k(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs, int warp,
-                            int lane, uint32_t* status PFC_PARAM) {
+__device__ bool pf_decode_k(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
+                            const ShiftTable& st, int warp, int lane, uint32_t* status PFC_PARAM) {
     switch (u.K) {
-        case 1: return pf_decode_unit<1, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
-        case 2: return pf_decode_unit<2, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
-        case 3: return pf_decode_unit<3, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
-        default: return pf_decode_unit<4, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, warp, lane, status PFC_FWD);
+        case 1: return pf_decode_unit<1, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, st, warp, lane, status PFC_FWD);
+        case 2: return pf_decode_unit<2, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, st, warp, lane, status PFC_FWD);
+        case 3: return pf_decode_unit<3, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, st, warp, lane, status PFC_FWD);
+        default: return pf_decode_unit<4, CB, MODE>(H, Abuf, Wring, u.ksteps, gs, st, warp, lane, status PFC_FWD);
     }
 }
 
 template <int CB>
 __device__ bool pf_decode_dispatch(PfHead& H, uint8_t* Abuf, const uint8_t* Wring, const PfUnit& u, uint32_t& gs,
-                                   int warp, int lane, uint32_t* status PFC_PARAM) {
-    return u.mode == 0 ? pf_decode_k<CB, 0>(H, Abuf, Wring, u, gs, warp, lane, status PFC_FWD)
-                       : pf_decode_k<CB, 1>(H, Abuf, Wring, u, gs, warp, lane, status PFC_FWD);
+                                   const ShiftTable& st, int warp, int lane, uint32_t* status PFC_PARAM) {
+    return u.mode == 0 ? pf_decode_k<CB, 0>(H, Abuf, Wring, u, gs, st, warp, lane, status PFC_FWD)
+                       : pf_decode_k<CB, 1>(H, Abuf, Wring, u, gs, st, warp, lane, status PFC_FWD);
 }
 
 // Unit of ticket `tk` (mode -1 once the tickets run out); ngu / ndn are
@@ -702,7 +712,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             __syncwarp();
             if (lane == 0) mbar_arrive(&H.dempty[d]);
             if (u.mode < 0) break;
-            if (!pf_decode_dispatch<CB>(H, Abuf, Wring, u, gs, warp, lane, status PFC_FWD)) break;
+            if (!pf_decode_dispatch<CB>(H, Abuf, Wring, u, gs, p.st, warp, lane, status PFC_FWD)) break;
         }
         PFC_FLUSH(PF_DEC_TOTAL, lane);
     } else {
@@ -1053,6 +1063,7 @@ static int moe_prefill_impl(const void* x, int x_dtype, void* out, int out_dtype
     for (int i = 0; i < 9; ++i) p.tab[i] = tabs[i];
     p.ktab = k_table;
     p.Kscalar = K;
+    shift_table_init(p.st);
     p.E = (int) n_experts;
     p.H = (int) hidden;
     p.I = (int) inter;

@@ -87,6 +87,7 @@ struct TcParams {
     const __half* svh;
     float* part;           // [chunks][M][n] fp32 partials
     uint32_t* status;
+    ShiftTable st;         // IMAD shift multipliers of the window extraction
 };
 
 
@@ -232,8 +233,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) linear_tc_kernel(const __grid_c
 #pragma unroll
             for (int i = i0; i < i0 + 2; ++i) {
                 const uint32_t* t = wst + (i * 8 + ntile) * F::WORDS;
-                uint32_t w[8], x[8];
-                tile_windows<K>(t, geom, w);
+                uint32_t whi[F::NG], wlo[F::NG], w[8], x[8];
+#pragma unroll
+                for (int h = 0; h < F::NG; ++h) {
+                    whi[h] = t[geom.ihi[h]];
+                    wlo[h] = t[geom.ilo[h]];
+                }
+                tile_windows_f<K>(whi, wlo, geom, p.st, w);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) x[j] = codebook_pair<CB>(w[j]);
                 const int kk = i * 16 + 2 * t4;
@@ -425,6 +431,7 @@ int linear_tc(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t n, co
     p.n = (int) n;
     p.svh = static_cast<const __half*>(svh);
     p.status = reinterpret_cast<uint32_t*>(sb) + 2;
+    shift_table_init(p.st);
     p.part = reinterpret_cast<float*>(sb + EXL3_LINEAR_CTRL_BYTES + align_up(rows * k * 2, 256));
     const int64_t items = rows * (k / 128);
     tc_input_kernel<<<(unsigned) ((items + 7) / 8), 256, 0, s>>>(x, x_dtype, (int) rows, (int) k,
