@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -932,11 +933,11 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
 namespace {
 
 // Number of k-chunks of a dimension of `n` elements: the smallest count
-// >= ceil(n / 1024) that splits it into whole 128-element blocks, at most
+// >= ceil(n / kchunk) that splits it into whole 128-element blocks, at most
 // `cap` (the largest such divisor otherwise).
-int chunks_for(int64_t n, int cap) {
+int chunks_for(int64_t n, int cap, int kchunk) {
     const int64_t blocks = n / 128;
-    const int lo = (int) ((n + 1023) / 1024);
+    const int lo = (int) ((n + kchunk - 1) / kchunk);
     for (int c = lo; c <= cap; ++c)
         if (blocks % c == 0) return c;
     for (int c = cap; c >= 1; --c)
@@ -950,13 +951,28 @@ struct MoeGeom {
     int64_t off_tmaps, off_partA, off_xg, off_ag, off_partB, off_downc, total;
 };
 
+// Target k-chunk of the units: 2048 when the gate/up units at that size alone
+// still give every CTA four or more -- long units pay their per-unit costs
+// (claim, tensor-map update, dependency check, partial hand-off) less often,
+// and with a single down chunk the down partials are finished from shared
+// memory (config 2: 200 -> 192 us per layer) -- else 1024: the TP shards,
+// whose few long units would leave CTAs idle (TP8: 44 -> 48 us at 2048).
+// `grid` 0 gives 1024, the choice that needs the most scratch.
+int moe_kchunk(int64_t m, int64_t topk, int64_t E, int64_t H, int64_t I, int grid) {
+    if (grid <= 0) return 1024;
+    const int64_t gmax = std::min<int64_t>(E, m * topk);
+    const int64_t units = gmax * (I / 128) * 2 * chunks_for(H, kMoeMaxNka, 2048);
+    return units >= 4 * (int64_t) grid ? 2048 : 1024;
+}
+
 // Scratch geometry (fragments sized for the fast path's 4 words per lane,
-// which the precise path's 2 words also fit).
-MoeGeom moe_geom(int64_t m, int64_t topk, int64_t H, int64_t I) {
+// which the precise path's 2 words also fit).  Fewer chunks never need more
+// scratch, so the 1024 geometry bounds every choice.
+MoeGeom moe_geom(int64_t m, int64_t topk, int64_t H, int64_t I, int kchunk = 1024) {
     MoeGeom g{};
-    g.nka = chunks_for(H, kMoeMaxNka);
+    g.nka = chunks_for(H, kMoeMaxNka, kchunk);
     g.kca = (int) (H / g.nka);
-    g.nkb = chunks_for(I, kMoeMaxNkb);
+    g.nkb = chunks_for(I, kMoeMaxNkb, kchunk);
     g.kcb = (int) (I / g.nkb);
     g.pairs = m * topk;
     int64_t off = EXL3_MOE_CTRL_BYTES;
@@ -1191,14 +1207,16 @@ int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_
     EXL3_REQUIRE(swiglu_limit > 0.0f && swiglu_limit < 3.0e38f, EXL3_ERR_ARG,
                  "moe: requires a finite positive SwiGLU limit");
     EXL3_REQUIRE(aligned16(scratch), EXL3_ERR_ARG, "moe: scratch must be 16-byte aligned");
-    const MoeGeom g = moe_geom(m, topk, hidden, inter);
-    EXL3_REQUIRE(scratch_bytes >= g.total, EXL3_ERR_ARG, "moe: scratch too small (%lld < %lld bytes)",
-                 (long long) scratch_bytes, (long long) g.total);
+    // the scratch is checked against exl3_moe_scratch_bytes (the most any k-chunk choice needs)
+    const int64_t need = moe_geom(m, topk, hidden, inter).total;
+    EXL3_REQUIRE(scratch_bytes >= need, EXL3_ERR_ARG, "moe: scratch too small (%lld < %lld bytes)",
+                 (long long) scratch_bytes, (long long) need);
+    MoePrepared pr;
+    if (int rc = moe_prepare_any(cb, precise != 0, &pr)) return rc;
+    const MoeGeom g = moe_geom(m, topk, hidden, inter, moe_kchunk(m, topk, n_experts, hidden, inter, pr.grid));
     EXL3_REQUIRE(g.kca % (kMoeSK * 16) == 0 && g.kcb % (kMoeSK * 16) == 0 && g.nka <= kMoeMaxNka &&
                      g.nkb <= kMoeMaxNkb, EXL3_ERR_UNSUPPORTED,
                  "moe: internal k-chunks (%d, %d) do not tile the ring stages", g.kca, g.kcb);
-    MoePrepared pr;
-    if (int rc = moe_prepare_any(cb, precise != 0, &pr)) return rc;
 
     MoeParams p{};
     p.x = x;
