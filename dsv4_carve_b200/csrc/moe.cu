@@ -280,9 +280,13 @@ constexpr int kMoeHeadBytes = (int) ((sizeof(MoeHead) + 127) / 128 * 128);
 // projection mat (0 gate, 1 up): fp16(x) * suh in fp16, 128-point Hadamard in
 // fp32, * 1/sqrt(128) -> fp16 (recipe-lna/lna2/lna_moe_ticket.cu:119-144),
 // written as B fragments.
+// The suh values are loaded once and the activations of four rows at a time
+// are in flight together, so the item costs about one load latency per four
+// rows rather than one per row (it is on the path to the layer's first units).
 template <bool PRECISE>
 __device__ void moe_input_item(const MoeParams& p, const MoePlan& P, int g, int mat, int kb, int lane) {
     constexpr int FW = Frag<PRECISE>::FW;
+    constexpr int kRowBatch = 4;
     const int e = P.gexp[g];
     uint32_t gm = P.gmask[g];
     const int nrows = __popc(gm), pair0 = P.gpair[g];
@@ -290,22 +294,35 @@ __device__ void moe_input_item(const MoeParams& p, const MoePlan& P, int g, int 
     const __half* suh = reinterpret_cast<const __half*>(p.tab[mat ? 4 : 1][e]);
     uint32_t* gbase = p.xg + (size_t) pair0 * 2 * HS * 4 * FW;
     const int k0 = kb * 128 + lane * 4;
-    for (int ri = 0; ri < nrows; ++ri) {
-        const int row = __ffs((int) gm) - 1;
-        gm &= gm - 1u;
-        float v[4];
+    __half su[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const __half a = load_act_half(p.x, p.x_dtype, (int64_t) row * p.H + k0 + q);
-            v[q] = __half2float(__hmul(a, suh[k0 + q]));
+    for (int q = 0; q < 4; ++q) su[q] = suh[k0 + q];
+    for (int r0 = 0; r0 < nrows; r0 += kRowBatch) {
+        __half xa[kRowBatch][4];
+#pragma unroll
+        for (int j = 0; j < kRowBatch; ++j) {
+            if (r0 + j < nrows) {
+                const int row = __ffs((int) gm) - 1;
+                gm &= gm - 1u;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) xa[j][q] = load_act_half(p.x, p.x_dtype, (int64_t) row * p.H + k0 + q);
+            }
         }
-        wht128_warp(v, lane);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int kl = lane * 4 + q;
-            const int ks = kb * 8 + (kl >> 4);
-            uint32_t* rs = gbase + ((size_t) (mat * HS + ks) * nrows + ri) * 4 * FW;
-            store_frag<PRECISE>(rs, kl & 15, __float2half_rn(v[q] * kHadNorm));
+        for (int j = 0; j < kRowBatch; ++j) {
+            if (r0 + j >= nrows) break;   // warp-uniform
+            const int ri = r0 + j;
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = __half2float(__hmul(xa[j][q], su[q]));
+            wht128_warp(v, lane);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int kl = lane * 4 + q;
+                const int ks = kb * 8 + (kl >> 4);
+                uint32_t* rs = gbase + ((size_t) (mat * HS + ks) * nrows + ri) * 4 * FW;
+                store_frag<PRECISE>(rs, kl & 15, __float2half_rn(v[q] * kHadNorm));
+            }
         }
     }
 }
@@ -323,15 +340,24 @@ __device__ void moe_finish_a(const MoeParams& p, const MoePlan& P, int g, int bl
     const __half* usv = reinterpret_cast<const __half*>(p.tab[5][e]) + blk * kCols;
     const __half* dsu = reinterpret_cast<const __half*>(p.tab[7][e]) + blk * kCols;
     uint32_t* abase = p.ag + (size_t) pair0 * IS * 4 * FW;
+    // the block's svh (gate, up) and down suh, loaded once for all rows
+    float gs[4], us[4];
+    __half ds[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        gs[q] = __half2float(gsv[lane * 4 + q]);
+        us[q] = __half2float(usv[lane * 4 + q]);
+        ds[q] = dsu[lane * 4 + q];
+    }
     for (int ri = 0; ri < nrows; ++ri) {
         const int64_t pr = pair0 + ri;
         float gv[4] = {0.f, 0.f, 0.f, 0.f}, uv[4] = {0.f, 0.f, 0.f, 0.f};
-        // two chunks of gate and of up at a time (four loads in flight), summed
-        // in chunk order
-        for (int c0 = 0; c0 < p.nka; c0 += 2) {
-            float4 a[2], b[2];
+        // four chunks of gate and of up at a time (eight loads in flight:
+        // one round for up to 4 chunks), summed in chunk order
+        for (int c0 = 0; c0 < p.nka; c0 += 4) {
+            float4 a[4], b[4];
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < 4; ++j)
                 if (c0 + j < p.nka) {
                     a[j] = __ldcg(reinterpret_cast<const float4*>(
                         p.partA + ((pr * 2 + 0) * p.nka + c0 + j) * p.I + blk * kCols + lane * 4));
@@ -339,23 +365,24 @@ __device__ void moe_finish_a(const MoeParams& p, const MoePlan& P, int g, int bl
                         p.partA + ((pr * 2 + 1) * p.nka + c0 + j) * p.I + blk * kCols + lane * 4));
                 }
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < 4; ++j)
                 if (c0 + j < p.nka) {
                     gv[0] += a[j].x; gv[1] += a[j].y; gv[2] += a[j].z; gv[3] += a[j].w;
                     uv[0] += b[j].x; uv[1] += b[j].y; uv[2] += b[j].z; uv[3] += b[j].w;
                 }
         }
-        out_transform(gv, gsv, lane);
-        out_transform(uv, usv, lane);
+        // output transform: H128, / sqrt(128), * svh (same float order as out_transform)
+        wht128_warp(gv, lane);
+        wht128_warp(uv, lane);
         float dv[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            float gg = gv[q], uu = uv[q];
+            float gg = gv[q] * kHadNorm * gs[q], uu = uv[q] * kHadNorm * us[q];
             if (gg > p.limit) gg = p.limit;
             if (uu < -p.limit) uu = -p.limit;
             if (uu > p.limit) uu = p.limit;
             const __half a = __float2half_rn((gg / (1.0f + __expf(-gg))) * uu);
-            dv[q] = __half2float(__hmul(a, dsu[lane * 4 + q]));
+            dv[q] = __half2float(__hmul(a, ds[q]));
         }
         wht128_warp(dv, lane);
 #pragma unroll
