@@ -179,6 +179,16 @@ __device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t* p, uint32_t v
     return old;
 }
 
+// Atomic add with acquire-release semantics at GPU scope: releases this
+// thread's earlier writes like atom_add_release_gpu and, for the thread that
+// learns from the old value that it completed a count, acquires what the
+// other adders released, without a separate fence.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Add without a return value, ordered after this thread's earlier writes
 // (and those a preceding warp or CTA barrier made it observe).
 __device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {

@@ -325,12 +325,10 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
             ++uu;
             int last = 0;
             if (lane == 0) {
-                const uint32_t old = atom_add_release_gpu(&cnt[blk], 1u);
+                // release this unit's partial; the last unit also acquires the others'
+                const uint32_t old = atom_add_acq_rel_gpu(&cnt[blk], 1u);
                 last = old == (uint32_t) (p.nk - 1);
-                if (last) {
-                    atomicExch(&cnt[blk], 0u);
-                    fence_acq_rel_gpu();
-                }
+                if (last) atomicExch(&cnt[blk], 0u);
             }
             if (uu == 1) LTL_MARK(4);
             last = __shfl_sync(0xffffffffu, last, 0);

@@ -64,7 +64,10 @@ constexpr int kNBImax = kMoeMaxInter / 128;
 constexpr int kNBHmax = kMoeMaxHidden / 128;
 // CTA roles: warps 0-7 consume (decode + MMA), warp 8 produces (tickets,
 // stage copies), warp 9 stores partials and runs the block epilogues.
-constexpr int kMoeClaimAhead = 4;    // ring stages still queued when the producer claims its next unit
+#ifndef EXL3_MOE_CLAIM_AHEAD
+#define EXL3_MOE_CLAIM_AHEAD 4
+#endif
+constexpr int kMoeClaimAhead = EXL3_MOE_CLAIM_AHEAD;   // ring stages still queued when the producer claims its next unit
 constexpr int kMoeConsumerWarps = 8;
 constexpr int kMoeProducerWarp = 8;
 constexpr int kMoeEpilogueWarp = 9;
@@ -805,12 +808,10 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 const uint32_t target = kind == 0 ? (uint32_t) (2 * p.nka) : (uint32_t) p.nkb;
                 // release this unit's partial (the whole warp's stores, ordered by
                 // the __syncwarp above)
-                const uint32_t old = atom_add_release_gpu(cnt, 1u);
+                // release this unit's partial; the last unit also acquires the others'
+                const uint32_t old = atom_add_acq_rel_gpu(cnt, 1u);
                 last = old == target - 1u;
-                if (last) {
-                    atomicExch(cnt, 0u);
-                    fence_acq_rel_gpu();   // acquire every unit's partial of the block
-                }
+                if (last) atomicExch(cnt, 0u);
             }
             last = __shfl_sync(0xffffffffu, last, 0);
             PHASE_MARK(PH_EPI_STORE);
@@ -821,7 +822,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 __syncwarp();
                 if (lane == 0) {
                     fence_proxy_async_global();   // release the down-input fragments
-                    atom_add_release_gpu(&readyB[g * kMoeMaxNkb + (blk * kCols) / p.kcb], 1u);
+                    red_add_release_gpu(&readyB[g * kMoeMaxNkb + (blk * kCols) / p.kcb], 1u);
                 }
                 PHASE_MARK(PH_FIN_A);
             } else {
@@ -851,7 +852,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             __syncwarp();
             if (lane == 0) {
                 fence_proxy_async_global();
-                atom_add_release_gpu(&readyP[(g * 2 + mat) * kMoeMaxNka + kb / (p.kca / kCols)], 1u);
+                red_add_release_gpu(&readyP[(g * 2 + mat) * kMoeMaxNka + kb / (p.kca / kCols)], 1u);
             }
         }
         PHASE_MARK(PH_P);
