@@ -64,10 +64,11 @@ constexpr int kNBImax = kMoeMaxInter / 128;
 constexpr int kNBHmax = kMoeMaxHidden / 128;
 // CTA roles: warps 0-7 consume (decode + MMA), warp 8 produces (tickets,
 // stage copies), warp 9 stores partials and runs the block epilogues.
-#ifndef EXL3_MOE_CLAIM_AHEAD
-#define EXL3_MOE_CLAIM_AHEAD 4
-#endif
-constexpr int kMoeClaimAhead = EXL3_MOE_CLAIM_AHEAD;   // ring stages still queued when the producer claims its next unit
+// Ring stages still queued when the producer claims its next unit: at most
+// this, and at most the shorter unit kind's stage count (TP8 shard: 2-stage
+// down units, where claiming later leaves the last units to idle CTAs:
+// 42.4 -> 41.5 us; config 2's 16-stage units want the deeper run-ahead).
+constexpr int kMoeClaimAhead = 4;
 constexpr int kMoeConsumerWarps = 8;
 constexpr int kMoeProducerWarp = 8;
 constexpr int kMoeEpilogueWarp = 9;
@@ -165,6 +166,7 @@ struct MoeParams {
     float limit;
     int kca, nka;               // gate/up k-chunk over H
     int kcb, nkb;               // down k-chunk over I
+    int claim_ahead;            // see kMoeClaimAhead
     RingGeom ring;              // ns stages of slot_bytes (weights: wpart bytes, then B fragments)
     uint32_t* ctrl;
     float* partA;               // [pairs][2][nka][I]
@@ -730,7 +732,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             int next_raw = total;
             if (lane == 0 && ok) {
                 const uint32_t ns = (uint32_t) p.ring.ns;
-                const uint32_t ahead = min((uint32_t) kMoeClaimAhead, ns - 2u);
+                const uint32_t ahead = min((uint32_t) p.claim_ahead, ns - 2u);
                 if (it > ahead) {
                     const uint32_t j = it - ahead - 1u;
                     ok = mbar_wait(&S.empty[j % ns], (j / ns) & 1u, status);
@@ -1265,6 +1267,7 @@ int moe_decode_impl(const void* x, int x_dtype, void* out, int out_dtype, int64_
     p.nka = g.nka;
     p.kcb = g.kcb;
     p.nkb = g.nkb;
+    p.claim_ahead = std::max(1, std::min({kMoeClaimAhead, g.kca / (16 * kMoeSK), g.kcb / (16 * kMoeSK)}));
     uint8_t* sb = static_cast<uint8_t*>(scratch);
     EXL3_REQUIRE(pr.grid <= kMoeMaxGrid, EXL3_ERR_UNSUPPORTED, "moe: grid %d above %d", pr.grid, kMoeMaxGrid);
     MoeTemplates tmpl;
