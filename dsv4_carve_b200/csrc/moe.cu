@@ -138,8 +138,18 @@ static __device__ unsigned long long g_phase[PH_N];
 #ifdef EXL3_TIMELINE
 static __device__ unsigned long long g_tl[320][8];
 #define TL_MARK(i) do { if ((threadIdx.x & 31) == 0) g_tl[blockIdx.x][i] = globaltimer_ns(); } while (0)
+// Per-unit marks, by ticket t: [0] descriptor published, [1] tensor map
+// ready, [2] input dependency met, [3] last stage issued, [4] consumer warp 0
+// starts the unit, [5] it ends the unit, [6] epilogue done with the unit,
+// [7] the CTA.  Read with exl3_unit_trace_read.
+constexpr int kUtMax = 8192;
+static __device__ unsigned long long g_ut[kUtMax][8];
+#define UT_MARK(t, i) do { if ((threadIdx.x & 31) == 0 && (t) >= 0 && (t) < kUtMax) g_ut[t][i] = globaltimer_ns(); } while (0)
+#define UT_CTA(t) do { if ((threadIdx.x & 31) == 0 && (t) >= 0 && (t) < kUtMax) g_ut[t][7] = blockIdx.x; } while (0)
 #else
 #define TL_MARK(i)
+#define UT_MARK(t, i)
+#define UT_CTA(t)
 #endif
 
 // Tensor maps: one 3-D map per (projection kind, K) describes an expert
@@ -273,7 +283,7 @@ struct alignas(128) MoeHead {
     uint64_t dqe[kMoeDQ];
     uint64_t pfull[2];          // partial tile written by the consumer warps
     uint64_t pempty[2];         // partial tile stored by the epilogue warp
-    int desc[kMoeDQ][8];        // kind, group, mat, block, chunk, K
+    int desc[kMoeDQ][8];        // kind, group, mat, block, chunk, K, ticket
     int last_cta;
     int retire_rank;            // order in which this CTA retired
     uint32_t tp_epoch;          // this launch's exchange epoch (fused TP sum)
@@ -648,11 +658,16 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 if (ok) {
 #pragma unroll
                     for (int q = 0; q < 6; ++q) S.desc[slot][q] = d[q];
+#ifdef EXL3_TIMELINE
+                    S.desc[slot][6] = ticket;
+#endif
                     mbar_arrive(&S.dqf[slot]);
                 }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             ++du;
+            UT_MARK(ticket, 0);
+            UT_CTA(ticket);
             PHASE_MARK(PH_PROD_DESC);
             if (d[0] < 0 || !ok) break;
             if (d[5] == 0) {
@@ -693,6 +708,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 if (lane == 0) tmap_acquire(gtm);
             }
             PHASE_MARK(PH_PROD_TMAP);
+            UT_MARK(ticket, 1);
             // The unit's input fragments must be complete before they are copied.
             if (lane == 0) {
                 if (kind == 0) wait_counter(&readyP[(g * 2 + mat) * kMoeMaxNka + s], (uint32_t) (p.kca / kCols), status);
@@ -700,6 +716,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 fence_proxy_async_global();
             }
             __syncwarp();
+            UT_MARK(ticket, 2);
             PHASE_MARK(PH_PROD_DEP);
             const uint32_t wbytes = (uint32_t) (kMoeSK * 8 * tb);
             const int bbytes = (int) (kMoeSK * rsb);
@@ -724,6 +741,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 ++it;
                 PHASE_MARK(PH_PROD_ISSUE);
             }
+            UT_MARK(ticket, 3);
             // Claim the next unit only once at most `ahead` stages of this CTA's
             // ring are unconsumed: a CTA with a long backlog leaves the last
             // tickets to idle CTAs instead of ending the layer late.  (Stage j is
@@ -763,6 +781,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             int d[6];
 #pragma unroll
             for (int q = 0; q < 6; ++q) d[q] = S.desc[slot][q];
+#ifdef EXL3_TIMELINE
+            const int tk_ = S.desc[slot][6];
+#endif
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
@@ -792,6 +813,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
                 }
                 ++uu;
                 PHASE_MARK(PH_FIN_B);
+                UT_MARK(tk_, 6);
                 continue;
             }
             for (int r = 0; r < nrows; ++r) {
@@ -817,6 +839,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             }
             last = __shfl_sync(0xffffffffu, last, 0);
             PHASE_MARK(PH_EPI_STORE);
+            UT_MARK(tk_, 6);
             if (!last) continue;
             if (kind == 0) {
                 PHASE_COUNT(PH_FINS_A);
@@ -869,6 +892,10 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             int d[6];
 #pragma unroll
             for (int q = 0; q < 6; ++q) d[q] = S.desc[slot][q];
+#ifdef EXL3_TIMELINE
+            const int tk_ = S.desc[slot][6];
+            if (warp == 0) UT_MARK(tk_, 4);
+#endif
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.dqe[slot]);
             ++du;
@@ -887,6 +914,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_kernel(const __grid_consta
             PHASE_MARK(PH_UNIT);
             PHASE_COUNT(PH_UNITS);
             if (!ok) break;
+#ifdef EXL3_TIMELINE
+            if (warp == 0) UT_MARK(tk_, 5);
+#endif
             // this warp's 16 columns into the partial tile: D fragment (ch gr, row 2t),
             // (gr, 2t+1), (gr+8, 2t), (gr+8, 2t+1)
             const int ps = (int) (uu & 1u);
@@ -1191,6 +1221,15 @@ extern "C" int exl3_timeline_read(unsigned long long* out, int n) {
     EXL3_REQUIRE(out && n >= 1 && n <= 320 * 8, EXL3_ERR_ARG, "timeline: bad output");
     EXL3_CUDA(cudaDeviceSynchronize());
     EXL3_CUDA(cudaMemcpyFromSymbol(out, exl3::g_tl, sizeof(unsigned long long) * n));
+    return EXL3_OK;
+}
+
+// Per-unit marks of the timeline build ([ticket][8], see UT_MARK); every
+// launch rewrites the marks of its tickets.
+extern "C" int exl3_unit_trace_read(unsigned long long* out, int n) {
+    EXL3_REQUIRE(out && n >= 1 && n <= exl3::kUtMax * 8, EXL3_ERR_ARG, "unit trace: bad output");
+    EXL3_CUDA(cudaDeviceSynchronize());
+    EXL3_CUDA(cudaMemcpyFromSymbol(out, exl3::g_ut, sizeof(unsigned long long) * n));
     return EXL3_OK;
 }
 #endif
