@@ -73,6 +73,7 @@ constexpr int kMoeConsumerWarps = 8;
 constexpr int kMoeProducerWarp = 8;
 constexpr int kMoeEpilogueWarp = 9;
 constexpr int kMoeThreads = 320;
+static_assert(kMoeMaxSlots <= kMoeThreads, "the route plan gives every slot its own thread");
 // Control region (uint32 words).  ctrl[0] unit ticket, [1] retired CTAs,
 // [2] status word, [3] unused.  Then the per-group counters.
 constexpr int kCtrlWords = 16;
@@ -210,13 +211,13 @@ struct MoePlan {
 __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
     const bool worker = tid < kConsumerThreads;      // 256 threads own 4 experts each
     const int nthr = (int) blockDim.x;
+    // thread s owns slot s (m * topk <= kMoeMaxSlots <= the block): its id is
+    // loaded once, ahead of the mask clearing, and reused for slot -> pair
+    const int nslots = p.m * p.topk;
+    const int my_id = tid < nslots ? route_local_id(p.route, tid, p.E) : -1;
     for (int e = tid; e < p.E; e += nthr) P.emask[e] = 0u;
     __syncthreads();
-    const int nslots = p.m * p.topk;
-    for (int s = tid; s < nslots; s += nthr) {
-        const int id = route_local_id(p.route, s, p.E);
-        if (id >= 0) atomicOr(&P.emask[id], 1u << (s / p.topk));
-    }
+    if (my_id >= 0) atomicOr(&P.emask[my_id], 1u << (tid / p.topk));
     __syncthreads();
     // Each worker thread owns experts [4t, 4t+4) (E <= 1024).
     const int warp = tid >> 5, lane = tid & 31;
@@ -263,14 +264,13 @@ __device__ void build_plan(MoePlan& P, const MoeParams& p, int tid) {
         if (tid == kConsumerThreads - 1) { P.G = gh; P.P = gp; }
     }
     __syncthreads();
-    for (int s = tid; s < nslots; s += nthr) {
-        const int id = route_local_id(p.route, s, p.E);
+    if (tid < nslots) {
         short sp = -1;
-        if (id >= 0) {
-            const int row = s / p.topk;
-            sp = (short) (P.epair[id] + __popc(P.emask[id] & ((1u << row) - 1u)));
+        if (my_id >= 0) {
+            const int row = tid / p.topk;
+            sp = (short) (P.epair[my_id] + __popc(P.emask[my_id] & ((1u << row) - 1u)));
         }
-        P.slotpair[s] = sp;
+        P.slotpair[tid] = sp;
     }
     __syncthreads();
 }
